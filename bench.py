@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""ViT-B/16 FP32-parity inference benchmark (images/sec @ bs256 per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...    (N > 1)
+
+A step is one forward of `batch` images per GPU (224x224 default: T=197) with
+seeded N(0,1) inputs and seeded random-init ViT-B/16 weights (synthetic data,
+no checkpoints offline). Weak scaling: every rank runs its own batch; for N > 1
+the logits are all-gathered with NCCL inside the step. Rank 0 prints one JSON
+line.
+
+  value     images/s over all ranks, inputs resident in HBM, CUDA events, max
+            over ranks. Inputs (154 MB/GPU at bs256) exceed L2 (126 MB).
+  e2e       the same through the public API ViTCUDA.forward with the step's
+            images copied host(pinned)->device and the logits read back to pinned
+            host memory inside the timed region.
+  roofline  the dominant kernel (the TF32x3 tcgen05 GEMM, fc1 shape of this
+            workload) timed with CUDA events on its stream; achieved = TF32
+            tensor-pipe FLOP/s (3 x 2MNK / t) against the dense TF32 peak of a
+            cuBLAS TF32 GEMM measured in the same run.
+  cpu_baseline  the CPU oracle (a PyTorch fp32 restatement of the reference
+            path) on the host cores, rank 0 at N=1, on a bounded sample.
+
+--impl reference times the reference path's CPU implementation (the oracle
+port; the reference project itself has no CPU path and its timm dependency is
+absent) on the same config and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "vit-engine-cuda_b200")
+for _p in (PKG, REPO):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "ViT-B/16 images/sec @bs256 per GPU (FP32 parity, TF32x3)"
+UNIT = "images/s"
+CONFIGS = {
+    # name: (images per GPU per step, image size)
+    "bs256_224": (256, 224),   # bs256 on one B200
+    "bs512_384": (512, 384),   # BASELINE configs[4] per-GPU shard (B=4096 over 8 GPUs)
+}
+GFLOP_PER_IMG = {224: 35.1277, 384: 110.9687}
+SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="bs256_224")
+    ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-p50", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def emit(obj):
+    print(json.dumps(obj), flush=True)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.lines = []
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={SMI_FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [[c.strip() for c in ln.split(",")] for ln in out.splitlines() if ln.strip()]
+        sm, smax, reasons = [], None, set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(names[1:], r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- helpers
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def timed(fn, steps, world, dev):
+    """CUDA-event time of `steps` calls of fn on the current stream, bracketed by
+    a barrier and a synchronize on both sides; max over ranks (ms)."""
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1), world, dev)
+
+
+def cuBLAS_tf32_peak(dev) -> float:
+    """Dense TF32 TFLOP/s of a cuBLAS 8192^3 matmul, best of 10 (burst)."""
+    n = 8192
+    a = torch.randn(n, n, device=dev)
+    b = torch.randn(n, n, device=dev)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for _ in range(3):
+            torch.matmul(a, b)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def gemm_roofline(dev, M: int, N: int, K: int, reps: int = 10):
+    """Times the TF32x3 GEMM (fc1 shape: bias + GELU, TF32-pair output) alone."""
+    from vit_cuda import _lib
+    lib = _lib.lib
+    s = torch.cuda.current_stream().cuda_stream
+    a = torch.randn(M, K, device=dev)
+    w = torch.randn(N, K, device=dev) * 0.02
+    bias = torch.randn(N, device=dev) * 0.02
+    ap = torch.empty(2, M, K, device=dev)
+    wp = torch.empty(2, N, K, device=dev)
+    _lib.check(lib.vitb200_split_tf32(a.data_ptr(), M, K, K, ap.data_ptr(), K, s), "split")
+    _lib.check(lib.vitb200_split_tf32(w.data_ptr(), N, K, K, wp.data_ptr(), K, s), "split")
+    del a
+    out = torch.empty(2, M, N, device=dev)
+
+    def launch():
+        _lib.check(lib.vitb200_gemm_pairs(ap.data_ptr(), wp.data_ptr(), bias.data_ptr(), None,
+                                          None, 0, out.data_ptr(), M, K, N, _lib.EPI_BIAS_GELU,
+                                          s), "gemm")
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del ap, wp, out
+    return ms
+
+
+def ncu_traffic(name: str):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", name)
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+def cpu_oracle_rate(img_size: int, sample: int, min_seconds: float = 10.0, max_reps: int = 20):
+    """Images/s of the CPU oracle (fp32) on `sample` images, repeated for at
+    least min_seconds (one repetition minimum)."""
+    from oracle import vit_oracle
+    from vit_cuda.weights import synthetic_images, synthetic_state_dict
+    torch.set_num_threads(os.cpu_count() or 1)
+    state = synthetic_state_dict(seed=0, img_size=img_size)
+    img = synthetic_images(sample, img_size, seed=0)
+    with torch.no_grad():
+        vit_oracle.vit_forward(img[:1], state, dtype=torch.float32)  # warm-up
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < max_reps:
+            vit_oracle.vit_forward(img, state, dtype=torch.float32)
+            reps += 1
+            if time.perf_counter() - t0 >= min_seconds:
+                break
+        dt = time.perf_counter() - t0
+    return sample * reps / dt, reps, torch.get_num_threads()
+
+
+# ----------------------------------------------------------------- arms
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    batch, img = CONFIGS[args.config]
+    from oracle import vit_oracle
+    from vit_cuda.weights import synthetic_images, synthetic_state_dict
+    torch.set_num_threads(os.cpu_count() or 1)
+    state = synthetic_state_dict(seed=0, img_size=img)
+    x = synthetic_images(args.cpu_sample, img, seed=0)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            vit_oracle.vit_forward(x, state, dtype=torch.float32)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            vit_oracle.vit_forward(x, state, dtype=torch.float32)
+        dt = time.perf_counter() - t0
+    rate = args.cpu_sample * args.steps / dt
+    sample = (f"{args.cpu_sample} images per step of the {args.config} workload "
+              f"({img}x{img}, fp32), CPU oracle port of the reference path")
+    emit({
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, "global_batch": batch * world, "img_size": img,
+                   "seq_len": (img // 16) ** 2 + 1, "parallelism": "host cores"},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    })
+
+
+def run_ours(args):
+    rank, local_rank, world = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    assert torch.cuda.is_available(), "bench.py needs CUDA devices"
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    import vit_cuda
+    from vit_cuda import _lib
+    from vit_cuda.parallel import gather_rows
+    from vit_cuda.weights import synthetic_images, synthetic_state_dict
+
+    batch, img = CONFIGS[args.config]
+    T = (img // 16) ** 2 + 1
+    total = batch * world
+    state = synthetic_state_dict(seed=0, img_size=img)
+    model = vit_cuda.ViTCUDA(state_dict={k: v.to(dev) for k, v in state.items()}).to(dev).eval()
+    model.prepare()
+    x_host = synthetic_images(batch, img, seed=1000 + rank)
+    x_dev = x_host.to(dev)
+
+    def step_device():
+        logits = model._forward_impl(x_dev)
+        if world > 1:
+            gather_rows(logits, total)
+
+    x_pin = x_host.pin_memory()
+    x_in = torch.empty_like(x_dev)
+    out_pin = torch.empty((total, model.num_classes), dtype=torch.float32).pin_memory()
+
+    def step_e2e():
+        x_in.copy_(x_pin, non_blocking=True)
+        logits = model(x_in)
+        if world > 1:
+            logits = gather_rows(logits, total)
+        out_pin.copy_(logits, non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step_device()
+            step_e2e()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in
+                              os.environ else local_rank)
+        n0 = _lib.lib.vitb200_launch_count()
+        ms = timed(step_device, args.steps, world, dev)
+        launches = _lib.lib.vitb200_launch_count() - n0
+        clk = clocks.stop()
+        ms_e2e = timed(step_e2e, args.steps, world, dev)
+    assert _lib.device_error() == 0, "a kernel reported a device error"
+
+    value = total * args.steps / (ms * 1e-3)
+    e2e_value = total * args.steps / (ms_e2e * 1e-3)
+    h2d = x_host.numel() * 4
+    d2h = total * model.num_classes * 4
+    del x_dev, x_in
+
+    # Roofline of the dominant kernel (TF32x3 GEMM, the fc1 launch of this workload).
+    M = batch * T
+    gemm_ms = gemm_roofline(dev, M, 3072, 768)
+    alg_flops = 2.0 * M * 3072 * 768
+    tf32_peak = cuBLAS_tf32_peak(dev)
+    achieved = 3 * alg_flops / (gemm_ms * 1e-3) / 1e12
+    traffic = ncu_traffic(f"gemm_tf32x3_fc1_{args.config}.json")
+    roofline = {
+        "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+        "frac": achieved / tf32_peak, "traffic": traffic,
+        "kernel": f"gemm_tf32x3 fc1 M={M} N=3072 K=768 (+bias+GELU, TF32-pair out)",
+        "kernel_ms": gemm_ms, "algorithmic_tflops": alg_flops / (gemm_ms * 1e-3) / 1e12,
+        "peak_source": "cuBLAS TF32 8192^3 dense matmul measured in this run (burst); "
+                       "achieved counts the 3 TF32 products of TF32x3",
+    }
+
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, "model": "ViT-B/16 (random init, seed 0)",
+                   "global_batch": total, "img_size": img, "seq_len": T,
+                   "parallelism": f"dp{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (%.0f MB per GPU per step)" % (h2d / 1e6),
+                   "gflop_per_image": GFLOP_PER_IMG.get(img)},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "clocks": clk,
+        "model_tflops": GFLOP_PER_IMG.get(img, 0) * value / 1e3,
+    }
+
+    if world == 1 and rank == 0 and not args.no_p50:
+        result["p50_bs1_ms"] = p50_bs1(state, img, dev)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        rate, reps, cores = cpu_oracle_rate(img, args.cpu_sample)
+        result["cpu_baseline"] = {
+            "value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{args.cpu_sample} images x {reps} reps of the {args.config} workload "
+                      "(CPU oracle port of the reference path, fp32)"}
+    if rank == 0:
+        emit(result)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def p50_bs1(state, img, dev, iters: int = 200) -> dict:
+    """Batch-1 latency: CUDA-graph replays (the reference's capture_graph path)
+    and eager calls, CUDA events per call, median."""
+    import vit_cuda
+    model = vit_cuda.ViTCUDA(state_dict={k: v.to(dev) for k, v in state.items()}).to(dev).eval()
+    x = torch.randn(1, 3, img, img, device=dev)
+
+    def lat(fn):
+        ts = []
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        for _ in range(iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    with torch.no_grad():
+        eager = lat(lambda: model(x))
+        model.capture_graph(x, num_warmup=3)
+        graph = lat(lambda: model(x))
+        model.release_graph()
+    return {"graph_ms": graph, "eager_ms": eager}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

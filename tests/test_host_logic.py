@@ -1,0 +1,94 @@
+"""Host-side logic that needs no GPU: weight generator, sharding arithmetic,
+the reference-compatible argument checks of the per-op API, model buffer names."""
+import pytest
+import torch
+
+import vit_cuda
+from vit_cuda import _C
+from vit_cuda.parallel import padded_rows, shard_bounds
+from vit_cuda.weights import num_tokens, synthetic_images, synthetic_state_dict
+
+
+def test_synthetic_state_dict_layout():
+    sd = synthetic_state_dict(seed=0, img_size=224)
+    assert sd["patch_embed.proj.weight"].shape == (768, 3, 16, 16)
+    assert sd["pos_embed"].shape == (1, 197, 768)
+    assert sd["cls_token"].shape == (1, 1, 768)
+    assert sd["blocks.11.attn.qkv.weight"].shape == (2304, 768)
+    assert sd["blocks.0.mlp.fc2.weight"].shape == (768, 3072)
+    assert sd["head.weight"].shape == (1000, 768)
+    w = sd["blocks.3.mlp.fc1.weight"]
+    assert abs(w.std().item() - 0.02) < 1e-3 and w.abs().max().item() < 2.0
+    assert torch.all(sd["blocks.5.norm2.weight"] == 1) and torch.all(sd["norm.bias"] == 0)
+    assert num_tokens(384) == 577
+    sd2 = synthetic_state_dict(seed=0, img_size=224)
+    assert all(torch.equal(sd[k], sd2[k]) for k in sd)
+
+
+def test_synthetic_images():
+    x = synthetic_images(2, 224, seed=0)
+    assert x.shape == (2, 3, 224, 224) and x.dtype == torch.float32
+    assert torch.equal(x, synthetic_images(2, 224, seed=0))
+
+
+@pytest.mark.parametrize("total,world", [(256, 1), (2048, 8), (4096, 8), (5, 2), (3, 4), (0, 2)])
+def test_shard_bounds_cover_exactly(total, world):
+    seen = []
+    for r in range(world):
+        s, e = shard_bounds(total, world, r)
+        assert 0 <= s <= e <= total
+        assert e - s <= padded_rows(total, world)
+        seen.extend(range(s, e))
+    assert seen == list(range(total))
+
+
+def test_shard_bounds_rejects_bad_rank():
+    with pytest.raises(ValueError):
+        shard_bounds(10, 2, 2)
+
+
+def test_ops_reject_cpu_tensors_like_the_reference():
+    """csrc/include/cuda_checks.h:21-50 of the reference: non-CUDA inputs raise."""
+    x = torch.randn(1, 4, 768)
+    g = torch.ones(768)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.layernorm_forward(x, g, g, 1e-6)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.gemm_bias(x, torch.randn(8, 768), torch.randn(8))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.flash_attn_2(x, x, x, 0.125)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.patch_embed(torch.randn(1, 3, 224, 224), torch.randn(768, 768))
+
+
+def test_package_surface():
+    for name in ["flash_attn_2", "patch_embed", "pos_encoding", "mlp_forward",
+                 "layernorm_forward", "classifier_forward", "qkv_proj", "gemm_bias"]:
+        assert callable(getattr(vit_cuda, name))
+        assert getattr(vit_cuda._C, name) is getattr(vit_cuda, name)
+
+
+def test_model_buffer_names_match_reference():
+    """Buffer names of vit_cuda/model.py:23-37,78-91 in the reference."""
+    sd = synthetic_state_dict(seed=0, img_size=224, depth=2)
+    m = vit_cuda.ViTCUDA(state_dict=sd)
+    names = set(dict(m.named_buffers()))
+    for n in ["patch_weight", "patch_bias", "cls_token", "pos_embed", "norm_gamma", "norm_beta",
+              "head_weight", "head_bias", "blocks.1.qkv_weight", "blocks.0.fc2_bias",
+              "blocks.1.norm1_gamma", "blocks.0.norm2_beta", "blocks.1.proj_weight"]:
+        assert n in names, n
+    assert m.cls_token.shape == (1, 768) and m.pos_embed.shape == (197, 768)
+    assert m.img_size == (224, 224) and len(m.blocks) == 2
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m.prepare()
+
+
+def test_model_384_geometry():
+    sd = synthetic_state_dict(seed=0, img_size=384, depth=1)
+    m = vit_cuda.ViTCUDA(state_dict=sd)
+    assert m.img_size == (384, 384) and m.pos_embed.shape == (577, 768)
+
+
+def test_model_requires_state_dict_without_timm():
+    with pytest.raises(RuntimeError):
+        vit_cuda.ViTCUDA(state_dict=None)

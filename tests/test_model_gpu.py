@@ -1,0 +1,123 @@
+"""End-to-end parity of the fused ViT-B/16 forward against the CPU oracle.
+
+Bar (north star): logits max-abs <= 1e-3, per-block relative L2 <= 1e-5
+(chained and teacher-forced), 100% top-1 agreement, on seeded N(0,1) images and
+seeded random-init weights. Also the reference's own end-to-end checks:
+batch>1 (tests/test_end_to_end.py:22-45 of the reference project) and CUDA
+graph == eager (tests/test_end_to_end.py:48-68).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import vit_oracle as orc
+from vit_cuda import ViTCUDA
+from vit_cuda.weights import synthetic_images, synthetic_state_dict
+
+pytestmark = pytest.mark.gpu
+
+LOGITS_ATOL = 1e-3
+BLOCK_REL_L2 = 1e-5
+
+
+@pytest.fixture(scope="module")
+def case224(cuda):
+    state = synthetic_state_dict(seed=0, img_size=224)
+    img = synthetic_images(2, 224, seed=0)
+    logits, inter = orc.vit_forward(img, state, return_intermediates=True)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    return state, img, logits, inter, model
+
+
+def test_logits_match_oracle(case224, cuda):
+    _, img, ref, _, model = case224
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    err = (out - ref).abs().max().item()
+    assert err <= LOGITS_ATOL, err
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
+def test_logits_match_golden(case224, cuda):
+    """The committed transformers-generated golden logits (tests/golden)."""
+    _, img, _, _, model = case224
+    g = np.load(__file__.replace("test_model_gpu.py", "golden/vit_e2e_golden.npz"))
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu().numpy()
+    assert np.abs(out - g["b2_224/logits"]).max() <= LOGITS_ATOL
+
+
+def test_blocks_chained(case224, cuda):
+    """Per-block relative L2 of the fused path run block by block from its own
+    embedding (errors accumulate as in the full forward)."""
+    _, img, ref_logits, inter, model = case224
+    x = model.embed(img.to(cuda))
+    assert orc.rel_l2(x.cpu(), inter["embed"]) <= BLOCK_REL_L2
+    worst = 0.0
+    for i, ref_block in enumerate(inter["blocks"]):
+        x = model.block(i, x)
+        worst = max(worst, orc.rel_l2(x.cpu(), ref_block))
+    assert worst <= BLOCK_REL_L2, worst
+    logits, feats = model.head(x)
+    assert (logits.double().cpu() - ref_logits).abs().max().item() <= LOGITS_ATOL
+    assert (feats.double().cpu() - inter["features"]).abs().max().item() <= LOGITS_ATOL
+
+
+def test_blocks_teacher_forced(case224, cuda):
+    """Each block fed the oracle's input for that block."""
+    _, _, _, inter, model = case224
+    inputs = [inter["embed"]] + inter["blocks"][:-1]
+    for i, (xin, xout) in enumerate(zip(inputs, inter["blocks"])):
+        y = model.block(i, xin.float().to(cuda))
+        assert orc.rel_l2(y.cpu(), xout) <= BLOCK_REL_L2, i
+
+
+def test_forward_features(case224, cuda):
+    _, img, _, inter, model = case224
+    with torch.no_grad():
+        f = model.forward_features(img.to(cuda)).double().cpu()
+    assert (f - inter["features"]).abs().max().item() <= LOGITS_ATOL
+
+
+def test_batch_rows_differ(case224, cuda):
+    """Batch > 1 must not collapse rows (the reference's Phase-5 bug class,
+    scratch/repro_bug.py:20-27)."""
+    _, _, _, _, model = case224
+    x = synthetic_images(4, 224, seed=7).to(cuda)
+    with torch.no_grad():
+        out = model(x)
+        single = torch.cat([model(x[i:i + 1]) for i in range(4)])
+    assert not torch.allclose(out[0], out[1])
+    torch.testing.assert_close(out, single, atol=0, rtol=0)
+
+
+def test_graph_matches_eager(cuda):
+    state = synthetic_state_dict(seed=1, img_size=224)
+    torch.manual_seed(1)
+    x = torch.randn(4, 3, 224, 224, device=cuda)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    with torch.no_grad():
+        eager = model(x).clone()
+    model.capture_graph(x, num_warmup=3)
+    with torch.no_grad():
+        graph = model(x)
+    torch.testing.assert_close(graph, eager, atol=0, rtol=0)
+    x2 = torch.randn(4, 3, 224, 224, device=cuda)
+    with torch.no_grad():
+        g2 = model(x2).clone()
+    model.release_graph()
+    with torch.no_grad():
+        e2 = model(x2)
+    torch.testing.assert_close(g2, e2, atol=0, rtol=0)
+
+
+def test_384_tokens577(cuda):
+    """384x384 input, T = 577 (the reference's kernels hardcode 224/197)."""
+    state = synthetic_state_dict(seed=1, img_size=384)
+    img = synthetic_images(1, 384, seed=1)
+    ref = orc.vit_forward(img, state)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))

@@ -1,0 +1,758 @@
+// C ABI of libvitb200.so (declared in include/vitb200.h): argument checks,
+// workspace carving, per-device set-up, and the whole-model forward that chains
+// the kernels on one stream.
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
+#include "engine.h"
+#include "vitb200.h"
+
+namespace vitb200 {
+
+// Device error word: kernels that give up on a bounded wait record a code here.
+static __device__ int g_error_word[4];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int status = 0;
+  int* err = nullptr;
+  int sms = 148;
+};
+
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+DeviceState* device_state(int* status) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *status = cuda_status(e);
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    *status = VITB200_E_UNSUPPORTED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    int st = cuda_status(cudaGetSymbolAddress(&p, g_error_word));
+    if (!st) st = cuda_status(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    if (!st) {
+      d.err = static_cast<int*>(p);
+      d.ready = true;  // gemm_prepare_device() below reads the SM count
+      st = gemm_prepare_device();
+      if (st) d.ready = false;
+    }
+    d.status = st;
+    if (st) {
+      *status = st;
+      return nullptr;
+    }
+  }
+  *status = 0;
+  return &d;
+}
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int round4(int v) { return (v + 3) / 4 * 4; }
+
+// Bump allocator over the caller's workspace; with base == nullptr it only
+// measures.
+struct Carve {
+  uint8_t* base;
+  size_t cap;
+  size_t off = 0;
+  float* take(size_t nfloats) {
+    off = align_up(off, 256);
+    float* p = base ? reinterpret_cast<float*>(base + off) : nullptr;
+    off += nfloats * sizeof(float);
+    return p;
+  }
+  bool fits() const { return off <= cap; }
+};
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int check_ready() {
+  int st = 0;
+  device_state(&st);
+  return st;
+}
+
+}  // namespace
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int* device_error_word() {
+  int st = 0;
+  DeviceState* d = device_state(&st);
+  return d ? d->err : nullptr;
+}
+
+int device_num_sms() {
+  int st = 0;
+  DeviceState* d = device_state(&st);
+  return d ? d->sms : 148;
+}
+
+}  // namespace vitb200
+
+using namespace vitb200;
+
+#define VITB200_GUARD_BEGIN try {
+#define VITB200_GUARD_END \
+  }                       \
+  catch (...) {           \
+    return VITB200_E_INVALID_ARG; \
+  }
+
+extern "C" {
+
+int vitb200_version(void) { return 100; }
+
+const char* vitb200_status_string(int status) {
+  switch (status) {
+    case VITB200_OK: return "ok";
+    case VITB200_E_INVALID_ARG: return "invalid argument";
+    case VITB200_E_UNSUPPORTED: return "unsupported shape or configuration";
+    case VITB200_E_WORKSPACE: return "workspace too small";
+    case VITB200_E_DEVICE_TIMEOUT: return "a kernel gave up on a bounded wait";
+    case VITB200_E_NO_TMA: return "tensor-map encoding unavailable or rejected";
+    case VITB200_E_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    default: break;
+  }
+  if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
+  return "unknown status";
+}
+
+int vitb200_init(void) {
+  VITB200_GUARD_BEGIN
+  return check_ready();
+  VITB200_GUARD_END
+}
+
+int vitb200_device_error(int* code, int clear) {
+  VITB200_GUARD_BEGIN
+  if (!code) return VITB200_E_INVALID_ARG;
+  int st = 0;
+  DeviceState* d = device_state(&st);
+  if (!d) return st;
+  st = cuda_status(cudaDeviceSynchronize());
+  if (st) return st;
+  int host = 0;
+  st = cuda_status(cudaMemcpy(&host, d->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st) return st;
+  *code = host;
+  if (clear) st = cuda_status(cudaMemset(d->err, 0, sizeof(int)));
+  return st;
+  VITB200_GUARD_END
+}
+
+int vitb200_num_sms(void) { return device_num_sms(); }
+
+uint64_t vitb200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int vitb200_set_gemm_variant(int variant) { return gemm_set_variant(variant); }
+
+int vitb200_split_tf32(const float* x, int64_t rows, int cols, int64_t ldx, float* pair, int ldp,
+                       void* stream) {
+  VITB200_GUARD_BEGIN
+  if (rows < 0 || cols < 0 || ldp < cols || ldp % 4 != 0 || ldx < cols)
+    return VITB200_E_INVALID_ARG;
+  if (rows > 0 && ldp > 0 && (!x || !pair)) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  return split_tf32_launch(x, rows, cols, ldx, pair, ldp, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+int vitb200_layernorm(const float* x, const float* gamma, const float* beta, float* y,
+                      int64_t rows, int E, float eps, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (rows < 0 || E <= 0 || !x || !gamma || !beta || !y) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  return layernorm_launch(x, E, gamma, beta, y, E, nullptr, 0, 0, rows, E, eps,
+                          as_stream(stream));
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- GEMM
+
+size_t vitb200_gemm_workspace_bytes(int64_t M, int K, int N) {
+  if (M < 0 || K < 0 || N < 0) return 0;
+  Carve c{nullptr, 0};
+  const int Kp = round4(K);
+  c.take(2 * static_cast<size_t>(M) * Kp);
+  c.take(2 * static_cast<size_t>(N) * Kp);
+  return align_up(c.off, 256);
+}
+
+static int epilogue_from_code(int code, const float* bias, const float* residual,
+                              GemmEpilogue* e) {
+  switch (code) {
+    case VITB200_EPI_NONE: break;
+    case VITB200_EPI_BIAS:
+      if (!bias) return VITB200_E_INVALID_ARG;
+      e->bias = bias;
+      break;
+    case VITB200_EPI_BIAS_GELU:
+      if (!bias) return VITB200_E_INVALID_ARG;
+      e->bias = bias;
+      e->gelu = 1;
+      break;
+    case VITB200_EPI_BIAS_RESID:
+      if (!bias || !residual) return VITB200_E_INVALID_ARG;
+      e->bias = bias;
+      e->residual = residual;
+      break;
+    default: return VITB200_E_INVALID_ARG;
+  }
+  return 0;
+}
+
+int vitb200_gemm(const float* X, const float* W, const float* bias, const float* residual,
+                 float* Y, int64_t M, int K, int N, int epilogue, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (M < 0 || K < 0 || N < 0) return VITB200_E_INVALID_ARG;
+  if (epilogue < VITB200_EPI_NONE || epilogue > VITB200_EPI_BIAS_RESID) return VITB200_E_INVALID_ARG;
+  if (M == 0 || N == 0) return 0;  // empty output: nothing to launch
+  GemmEpilogue e;
+  if (int st = epilogue_from_code(epilogue, bias, residual, &e)) return st;
+  if (!Y || (K > 0 && (!X || !W))) return VITB200_E_INVALID_ARG;
+  const int Kp = round4(K);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* ap = c.take(2 * static_cast<size_t>(M) * Kp);
+  float* wp = c.take(2 * static_cast<size_t>(N) * Kp);
+  if (K > 0 && (!workspace || !c.fits())) return VITB200_E_WORKSPACE;
+  if (int st = check_ready()) return st;
+  cudaStream_t s = as_stream(stream);
+  if (K > 0) {
+    if (int st = split_tf32_launch(X, M, K, K, ap, Kp, s)) return st;
+    if (int st = split_tf32_launch(W, N, K, K, wp, Kp, s)) return st;
+  }
+  GemmProblem p;
+  p.a_pair = ap;
+  p.b_pair = wp;
+  p.M = M;
+  p.N = N;
+  p.Kp = K > 0 ? Kp : 0;
+  e.ldr = N;
+  e.out = Y;
+  e.ldo = N;
+  p.epi = e;
+  return gemm_pairs_launch(p, s);
+  VITB200_GUARD_END
+}
+
+int vitb200_gemm_pairs(const float* a_pair, const float* w_pair, const float* bias,
+                       const float* residual, float* Y, int64_t ldy, float* y_pair, int64_t M,
+                       int Kp, int N, int epilogue, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (M < 0 || Kp < 0 || N < 0 || Kp % 4) return VITB200_E_INVALID_ARG;
+  if (epilogue < VITB200_EPI_NONE || epilogue > VITB200_EPI_BIAS_RESID) return VITB200_E_INVALID_ARG;
+  if (M == 0 || N == 0) return 0;
+  GemmEpilogue e;
+  if (int st = epilogue_from_code(epilogue, bias, residual, &e)) return st;
+  if (!Y && !y_pair) return VITB200_E_INVALID_ARG;
+  if (Y && ldy < N) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  GemmProblem p;
+  p.a_pair = a_pair;
+  p.b_pair = w_pair;
+  p.M = M;
+  p.N = N;
+  p.Kp = Kp;
+  e.ldr = N;
+  e.out = Y;
+  e.ldo = ldy;
+  e.out_pair = y_pair;
+  e.ldp = N;
+  e.pair_plane = M * static_cast<int64_t>(N);
+  p.epi = e;
+  return gemm_pairs_launch(p, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- QKV
+
+size_t vitb200_qkv_workspace_bytes(int64_t M, int E) {
+  return vitb200_gemm_workspace_bytes(M, E, 3 * E);
+}
+
+int vitb200_qkv(const float* X, const float* W, const float* b, float* qkv_out, int64_t M, int E,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (M < 0 || E <= 0 || !b) return VITB200_E_INVALID_ARG;
+  if (E % 32) return VITB200_E_UNSUPPORTED;
+  if (M == 0) return 0;
+  if (!X || !W || !qkv_out) return VITB200_E_INVALID_ARG;
+  const int N = 3 * E, Kp = round4(E);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* ap = c.take(2 * static_cast<size_t>(M) * Kp);
+  float* wp = c.take(2 * static_cast<size_t>(N) * Kp);
+  if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
+  if (int st = check_ready()) return st;
+  cudaStream_t s = as_stream(stream);
+  if (int st = split_tf32_launch(X, M, E, E, ap, Kp, s)) return st;
+  if (int st = split_tf32_launch(W, N, E, E, wp, Kp, s)) return st;
+  GemmProblem p;
+  p.a_pair = ap;
+  p.b_pair = wp;
+  p.M = M;
+  p.N = N;
+  p.Kp = Kp;
+  p.epi.bias = b;
+  p.epi.out = qkv_out;
+  p.epi.ldo = E;
+  p.epi.mode = kModeSplit3;
+  p.epi.e_split = E;
+  p.epi.split_plane = M * static_cast<int64_t>(E);
+  return gemm_pairs_launch(p, s);
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- MLP
+
+size_t vitb200_mlp_workspace_bytes(int64_t M, int E, int E4) {
+  if (M < 0 || E < 0 || E4 < 0) return 0;
+  Carve c{nullptr, 0};
+  const int K1 = round4(E), K2 = round4(E4);
+  c.take(2 * static_cast<size_t>(M) * K1);
+  c.take(2 * static_cast<size_t>(E4) * K1);
+  c.take(2 * static_cast<size_t>(E) * K2);
+  c.take(2 * static_cast<size_t>(M) * K2);
+  return align_up(c.off, 256);
+}
+
+int vitb200_mlp(const float* X, const float* W1, const float* b1, const float* W2,
+                const float* b2, float* H, float* O, int64_t M, int E, int E4, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (M < 0 || E <= 0 || E4 <= 0 || !b1 || !b2) return VITB200_E_INVALID_ARG;
+  if (M == 0) return 0;
+  if (!X || !W1 || !W2 || !H || !O) return VITB200_E_INVALID_ARG;
+  const int K1 = round4(E), K2 = round4(E4);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* xp = c.take(2 * static_cast<size_t>(M) * K1);
+  float* w1p = c.take(2 * static_cast<size_t>(E4) * K1);
+  float* w2p = c.take(2 * static_cast<size_t>(E) * K2);
+  float* hp = c.take(2 * static_cast<size_t>(M) * K2);
+  if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
+  if (int st = check_ready()) return st;
+  cudaStream_t s = as_stream(stream);
+  if (int st = split_tf32_launch(X, M, E, E, xp, K1, s)) return st;
+  if (int st = split_tf32_launch(W1, E4, E, E, w1p, K1, s)) return st;
+  if (int st = split_tf32_launch(W2, E, E4, E4, w2p, K2, s)) return st;
+  GemmProblem p1;
+  p1.a_pair = xp;
+  p1.b_pair = w1p;
+  p1.M = M;
+  p1.N = E4;
+  p1.Kp = K1;
+  p1.epi.bias = b1;
+  p1.epi.gelu = 1;
+  p1.epi.out = H;
+  p1.epi.ldo = E4;
+  if (K2 == E4) {  // the epilogue writes the hidden pair directly
+    p1.epi.out_pair = hp;
+    p1.epi.ldp = K2;
+    p1.epi.pair_plane = M * static_cast<int64_t>(K2);
+  }
+  if (int st = gemm_pairs_launch(p1, s)) return st;
+  if (K2 != E4) {
+    if (int st = split_tf32_launch(H, M, E4, E4, hp, K2, s)) return st;
+  }
+  GemmProblem p2;
+  p2.a_pair = hp;
+  p2.b_pair = w2p;
+  p2.M = M;
+  p2.N = E;
+  p2.Kp = K2;
+  p2.epi.bias = b2;
+  p2.epi.out = O;
+  p2.epi.ldo = E;
+  return gemm_pairs_launch(p2, s);
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- attention
+
+int vitb200_attention(const float* q, const float* k, const float* v, float* o, int B, int T,
+                      int heads, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, float scale,
+                      void* stream) {
+  VITB200_GUARD_BEGIN
+  if (B < 0 || T < 0 || heads <= 0 || !q || !k || !v || !o) return VITB200_E_INVALID_ARG;
+  const int64_t width = static_cast<int64_t>(heads) * 64;
+  if (ldq < width || ldk < width || ldv < width || ldo < width) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  return attention_launch(q, k, v, ldq, ldk, ldv, o, ldo, nullptr, 0, 0, B, T, heads, scale,
+                          as_stream(stream));
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- patch embed
+
+size_t vitb200_patch_embed_workspace_bytes(int B, int C, int H, int W, int E) {
+  if (B < 0 || C <= 0 || H < 16 || W < 16 || E <= 0) return 0;
+  Carve c{nullptr, 0};
+  const int64_t Mp = static_cast<int64_t>(B) * (H / 16) * (W / 16);
+  const int K = C * 256;
+  c.take(2 * static_cast<size_t>(Mp) * K);
+  c.take(2 * static_cast<size_t>(E) * K);
+  return align_up(c.off, 256);
+}
+
+int vitb200_patch_embed(const float* img, const float* weights, const float* bias, float* out,
+                        int B, int C, int H, int W, int E, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (B < 0 || C <= 0 || E <= 0 || H < 16 || W < 16 || H % 16 || W % 16)
+    return VITB200_E_INVALID_ARG;
+  if (B == 0) return 0;
+  if (!img || !weights || !out) return VITB200_E_INVALID_ARG;
+  const int64_t Mp = static_cast<int64_t>(B) * (H / 16) * (W / 16);
+  const int K = C * 256;
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* ap = c.take(2 * static_cast<size_t>(Mp) * K);
+  float* wp = c.take(2 * static_cast<size_t>(E) * K);
+  if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
+  if (int st = check_ready()) return st;
+  cudaStream_t s = as_stream(stream);
+  if (int st = im2col_pair_launch(img, B, C, H, W, ap, s)) return st;
+  if (int st = split_tf32_launch(weights, E, K, K, wp, K, s)) return st;
+  GemmProblem p;
+  p.a_pair = ap;
+  p.b_pair = wp;
+  p.M = Mp;
+  p.N = E;
+  p.Kp = K;
+  p.epi.bias = bias;  // optional, as in patch_embed_wrapper.cpp:46-48
+  p.epi.out = out;
+  p.epi.ldo = E;
+  return gemm_pairs_launch(p, s);
+  VITB200_GUARD_END
+}
+
+int vitb200_pos_encoding(const float* patches, const float* cls, const float* pos, float* out,
+                         int B, int P, int E, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (B < 0 || P < 0 || E <= 0 || !cls || !pos || !out) return VITB200_E_INVALID_ARG;
+  if (!patches && B > 0 && P > 0) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  return cls_pos_launch(cls, E, pos, patches, out, B, P, E, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- classifier
+
+size_t vitb200_classifier_workspace_bytes(int B, int E, int C) {
+  return vitb200_gemm_workspace_bytes(B, E, C);
+}
+
+int vitb200_classifier(const float* X, const float* W, const float* bias, float* logits, int B,
+                       int T, int E, int C, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  VITB200_GUARD_BEGIN
+  if (B < 0 || T <= 0 || E <= 0 || C < 0 || !bias) return VITB200_E_INVALID_ARG;
+  if (B == 0 || C == 0) return 0;
+  if (!X || !W || !logits) return VITB200_E_INVALID_ARG;
+  const int Kp = round4(E);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* ap = c.take(2 * static_cast<size_t>(B) * Kp);
+  float* wp = c.take(2 * static_cast<size_t>(C) * Kp);
+  if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
+  if (int st = check_ready()) return st;
+  cudaStream_t s = as_stream(stream);
+  // CLS rows are every T-th row of X.
+  if (int st = split_tf32_launch(X, B, E, static_cast<int64_t>(T) * E, ap, Kp, s)) return st;
+  if (int st = split_tf32_launch(W, C, E, E, wp, Kp, s)) return st;
+  GemmProblem p;
+  p.a_pair = ap;
+  p.b_pair = wp;
+  p.M = B;
+  p.N = C;
+  p.Kp = Kp;
+  p.epi.bias = bias;
+  p.epi.out = logits;
+  p.epi.ldo = C;
+  return gemm_pairs_launch(p, s);
+  VITB200_GUARD_END
+}
+
+// ---------------------------------------------------------------- model
+
+namespace {
+
+struct VitDims {
+  int P, T, Kpatch;
+  int64_t M, Mp;
+};
+
+int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
+  if (!p || batch < 0) return VITB200_E_INVALID_ARG;
+  if (p->embed_dim != 768 || p->num_heads * 64 != p->embed_dim || p->patch != 16)
+    return VITB200_E_UNSUPPORTED;
+  if (p->depth <= 0 || p->mlp_dim <= 0 || p->mlp_dim % 32 || p->in_chans <= 0 ||
+      p->num_classes < 0)
+    return VITB200_E_INVALID_ARG;
+  if (p->img_h < 16 || p->img_w < 16 || p->img_h % 16 || p->img_w % 16)
+    return VITB200_E_INVALID_ARG;
+  if (!p->patch_w_pair || !p->patch_b || !p->cls_token || !p->pos_embed || !p->blocks ||
+      !p->norm_w || !p->norm_b)
+    return VITB200_E_INVALID_ARG;
+  for (int i = 0; i < p->depth; ++i) {
+    const vitb200_block_params& b = p->blocks[i];
+    if (!b.norm1_w || !b.norm1_b || !b.qkv_w_pair || !b.qkv_b || !b.proj_w_pair || !b.proj_b ||
+        !b.norm2_w || !b.norm2_b || !b.fc1_w_pair || !b.fc1_b || !b.fc2_w_pair || !b.fc2_b)
+      return VITB200_E_INVALID_ARG;
+  }
+  d->P = (p->img_h / 16) * (p->img_w / 16);
+  d->T = d->P + 1;
+  d->Kpatch = p->in_chans * 256;
+  d->M = static_cast<int64_t>(batch) * d->T;
+  d->Mp = static_cast<int64_t>(batch) * d->P;
+  return 0;
+}
+
+// Workspace regions of the forward. x is the residual stream [M][768];
+// pair_a holds the im2col pair, then per block the LN1 / attention / LN2 pairs;
+// qkv [M][2304]; hpair the GELU output pair [2][M][mlp]; cls_pair the final
+// LN of the CLS rows.
+struct VitBuffers {
+  float *x, *pair_a, *qkv, *hpair, *cls_pair;
+};
+
+size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve* c,
+                 VitBuffers* b) {
+  const size_t D = static_cast<size_t>(p->embed_dim);
+  b->x = c->take(static_cast<size_t>(d.M) * D);
+  b->pair_a = c->take(2 * std::max(static_cast<size_t>(d.M) * D,
+                                   static_cast<size_t>(d.Mp) * d.Kpatch));
+  b->qkv = c->take(static_cast<size_t>(d.M) * 3 * D);
+  b->hpair = c->take(2 * static_cast<size_t>(d.M) * p->mlp_dim);
+  b->cls_pair = c->take(2 * static_cast<size_t>(batch) * D);
+  return align_up(c->off, 256);
+}
+
+// patches -> TF32 pair; patch GEMM with bias and positional rows fused into the
+// epilogue (rows b*T+1+p); CLS rows cls + pos[0]. Writes x[B*T][768].
+int vit_embed(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b,
+              const float* img, float* x, int batch, cudaStream_t s) {
+  const int D = p->embed_dim;
+  if (int st = im2col_pair_launch(img, batch, p->in_chans, p->img_h, p->img_w, b.pair_a, s))
+    return st;
+  GemmProblem g;
+  g.a_pair = b.pair_a;
+  g.b_pair = p->patch_w_pair;
+  g.M = d.Mp;
+  g.N = D;
+  g.Kp = d.Kpatch;
+  g.epi.bias = p->patch_b;
+  g.epi.out = x;
+  g.epi.ldo = D;
+  g.epi.mode = kModePatch;
+  g.epi.P = d.P;
+  g.epi.T = d.T;
+  g.epi.pos = p->pos_embed;
+  if (int st = gemm_pairs_launch(g, s)) return st;
+  return cls_pos_launch(p->cls_token, 0, p->pos_embed, nullptr, x, batch, d.P, D, s);
+}
+
+// One pre-LN encoder block in place on x (vit_cuda/model.py:39-60 order):
+// x += proj(attn(LN1 x)); x += fc2(GELU(fc1(LN2 x))). Residual adds are fused
+// into the proj / fc2 epilogues.
+int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, int layer,
+              float* x, int batch, cudaStream_t s) {
+  const int D = p->embed_dim;
+  const int64_t M = d.M;
+  const int64_t plane = M * D;
+  const vitb200_block_params& w = p->blocks[layer];
+  if (int st = layernorm_launch(x, D, w.norm1_w, w.norm1_b, nullptr, 0, b.pair_a, D, plane, M, D,
+                                p->ln_eps, s))
+    return st;
+  {
+    GemmProblem g;
+    g.a_pair = b.pair_a;
+    g.b_pair = w.qkv_w_pair;
+    g.M = M;
+    g.N = 3 * D;
+    g.Kp = D;
+    g.epi.bias = w.qkv_b;
+    g.epi.out = b.qkv;
+    g.epi.ldo = 3 * D;
+    if (int st = gemm_pairs_launch(g, s)) return st;
+  }
+  if (int st = attention_launch(b.qkv, b.qkv + D, b.qkv + 2 * D, 3 * D, 3 * D, 3 * D, nullptr, 0,
+                                b.pair_a, D, plane, batch, d.T, p->num_heads, p->attn_scale, s))
+    return st;
+  {
+    GemmProblem g;
+    g.a_pair = b.pair_a;
+    g.b_pair = w.proj_w_pair;
+    g.M = M;
+    g.N = D;
+    g.Kp = D;
+    g.epi.bias = w.proj_b;
+    g.epi.residual = x;
+    g.epi.ldr = D;
+    g.epi.out = x;
+    g.epi.ldo = D;
+    if (int st = gemm_pairs_launch(g, s)) return st;
+  }
+  if (int st = layernorm_launch(x, D, w.norm2_w, w.norm2_b, nullptr, 0, b.pair_a, D, plane, M, D,
+                                p->ln_eps, s))
+    return st;
+  {
+    GemmProblem g;
+    g.a_pair = b.pair_a;
+    g.b_pair = w.fc1_w_pair;
+    g.M = M;
+    g.N = p->mlp_dim;
+    g.Kp = D;
+    g.epi.bias = w.fc1_b;
+    g.epi.gelu = 1;
+    g.epi.out_pair = b.hpair;
+    g.epi.ldp = p->mlp_dim;
+    g.epi.pair_plane = M * p->mlp_dim;
+    if (int st = gemm_pairs_launch(g, s)) return st;
+  }
+  GemmProblem g;
+  g.a_pair = b.hpair;
+  g.b_pair = w.fc2_w_pair;
+  g.M = M;
+  g.N = D;
+  g.Kp = p->mlp_dim;
+  g.epi.bias = w.fc2_b;
+  g.epi.residual = x;
+  g.epi.ldr = D;
+  g.epi.out = x;
+  g.epi.ldo = D;
+  return gemm_pairs_launch(g, s);
+}
+
+// Final LayerNorm on the CLS rows only (the head reads token 0 alone), then
+// the head GEMM. features / logits may each be null.
+int vit_head(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, const float* x,
+             float* logits, float* features, int batch, cudaStream_t s) {
+  const int D = p->embed_dim;
+  const int64_t cls_stride = static_cast<int64_t>(d.T) * D;
+  const bool want_logits = logits != nullptr && p->num_classes > 0;
+  if (!features && !want_logits) return 0;
+  if (int st = layernorm_launch(x, cls_stride, p->norm_w, p->norm_b, features, D,
+                                want_logits ? b.cls_pair : nullptr, D,
+                                static_cast<int64_t>(batch) * D, batch, D, p->ln_eps, s))
+    return st;
+  if (!want_logits) return 0;
+  GemmProblem g;
+  g.a_pair = b.cls_pair;
+  g.b_pair = p->head_w_pair;
+  g.M = batch;
+  g.N = p->num_classes;
+  g.Kp = D;
+  g.epi.bias = p->head_b;
+  g.epi.out = logits;
+  g.epi.ldo = p->num_classes;
+  return gemm_pairs_launch(g, s);
+}
+
+// Shared prologue of the model entry points: checks, device set-up, carving.
+int vit_prepare(const vitb200_vit_params* p, int batch, void* workspace, size_t workspace_bytes,
+                VitDims* d, VitBuffers* b) {
+  if (int st = check_params(p, batch, d)) return st;
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  carve_vit(p, *d, batch, &c, b);
+  if (batch > 0 && (!workspace || !c.fits())) return VITB200_E_WORKSPACE;
+  return check_ready();
+}
+
+}  // namespace
+
+size_t vitb200_vit_workspace_bytes(const vitb200_vit_params* p, int batch) {
+  VitDims d;
+  if (check_params(p, batch, &d)) return 0;
+  Carve c{nullptr, 0};
+  VitBuffers b;
+  return carve_vit(p, d, batch, &c, &b);
+}
+
+int vitb200_vit_forward(const vitb200_vit_params* p, const float* img, float* logits, int batch,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (!logits || !img) return VITB200_E_INVALID_ARG;
+  if (p && (!p->head_w_pair || !p->head_b)) return VITB200_E_INVALID_ARG;
+  VitDims d;
+  VitBuffers b;
+  if (int st = vit_prepare(p, batch, workspace, workspace_bytes, &d, &b)) return st;
+  if (batch == 0) return 0;
+  cudaStream_t s = as_stream(stream);
+  if (int st = vit_embed(p, d, b, img, b.x, batch, s)) return st;
+  for (int i = 0; i < p->depth; ++i)
+    if (int st = vit_block(p, d, b, i, b.x, batch, s)) return st;
+  return vit_head(p, d, b, b.x, logits, nullptr, batch, s);
+  VITB200_GUARD_END
+}
+
+int vitb200_vit_forward_features(const vitb200_vit_params* p, const float* img, float* features,
+                                 int batch, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  VITB200_GUARD_BEGIN
+  if (!features || !img) return VITB200_E_INVALID_ARG;
+  VitDims d;
+  VitBuffers b;
+  if (int st = vit_prepare(p, batch, workspace, workspace_bytes, &d, &b)) return st;
+  if (batch == 0) return 0;
+  cudaStream_t s = as_stream(stream);
+  if (int st = vit_embed(p, d, b, img, b.x, batch, s)) return st;
+  for (int i = 0; i < p->depth; ++i)
+    if (int st = vit_block(p, d, b, i, b.x, batch, s)) return st;
+  return vit_head(p, d, b, b.x, nullptr, features, batch, s);
+  VITB200_GUARD_END
+}
+
+int vitb200_vit_embed(const vitb200_vit_params* p, const float* img, float* x, int batch,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (!img || !x) return VITB200_E_INVALID_ARG;
+  VitDims d;
+  VitBuffers b;
+  if (int st = vit_prepare(p, batch, workspace, workspace_bytes, &d, &b)) return st;
+  if (batch == 0) return 0;
+  return vit_embed(p, d, b, img, x, batch, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+int vitb200_vit_block(const vitb200_vit_params* p, int layer, float* x, int batch,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (!x || !p || layer < 0 || layer >= p->depth) return VITB200_E_INVALID_ARG;
+  VitDims d;
+  VitBuffers b;
+  if (int st = vit_prepare(p, batch, workspace, workspace_bytes, &d, &b)) return st;
+  if (batch == 0) return 0;
+  return vit_block(p, d, b, layer, x, batch, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+int vitb200_vit_head(const vitb200_vit_params* p, const float* x, float* logits,
+                     float* features, int batch, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  VITB200_GUARD_BEGIN
+  if (!x || (!logits && !features)) return VITB200_E_INVALID_ARG;
+  if (p && logits && (!p->head_w_pair || !p->head_b)) return VITB200_E_INVALID_ARG;
+  VitDims d;
+  VitBuffers b;
+  if (int st = vit_prepare(p, batch, workspace, workspace_bytes, &d, &b)) return st;
+  if (batch == 0) return 0;
+  return vit_head(p, d, b, x, logits, features, batch, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+}  // extern "C"

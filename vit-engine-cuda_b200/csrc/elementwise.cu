@@ -1,0 +1,306 @@
+// HBM-bound kernels of the ViT path: TF32 split, LayerNorm (fp32 and/or TF32
+// pair output), patch im2col into a TF32 pair, CLS + positional rows, and the
+// epilogue-only GEMM for K = 0.
+#include <algorithm>
+
+#include "common.cuh"
+#include "engine.h"
+#include "vitb200.h"
+
+namespace vitb200 {
+
+namespace {
+
+inline int grid_for(int64_t work, int threads) {
+  const int64_t per_sm = 2048 / threads;
+  const int64_t cap = static_cast<int64_t>(device_num_sms()) * per_sm * 4;
+  const int64_t g = (work + threads - 1) / threads;
+  return static_cast<int>(std::max<int64_t>(1, std::min(g, cap)));
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ split
+// pair[2][rows][ldp] <- TF32 hi/lo of x[rows][cols] (row stride ldx), zero pad.
+__global__ void split_tf32_kernel(const float* __restrict__ x, int64_t rows, int cols,
+                                  int64_t ldx, float* __restrict__ pair, int ldp, int vec_in) {
+  const int q_per_row = ldp / 4;
+  const int64_t total = rows * q_per_row;
+  const int64_t plane = rows * ldp;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / q_per_row;
+    const int c0 = static_cast<int>(i - r * q_per_row) * 4;
+    const float* src = x + r * ldx + c0;
+    float v[4];
+    if (vec_in && c0 + 4 <= cols) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (c0 + j < cols) ? src[j] : 0.f;
+    }
+    float hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tf32_split(v[j], hi[j], lo[j]);
+    float* dst = pair + r * ldp + c0;
+    *reinterpret_cast<float4*>(dst) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<float4*>(dst + plane) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+int split_tf32_launch(const float* x, int64_t rows, int cols, int64_t ldx, float* pair, int ldp,
+                      cudaStream_t s) {
+  if (rows < 0 || cols < 0 || ldp < cols || ldp % 4 != 0 || ldx < cols)
+    return VITB200_E_INVALID_ARG;
+  if (rows == 0 || ldp == 0) return 0;
+  if (!x || !pair) return VITB200_E_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(pair) % 16) return VITB200_E_ALIGNMENT;
+  const int vec_in = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 4 == 0);
+  const int64_t work = rows * (ldp / 4);
+  split_tf32_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, rows, cols, ldx, pair, ldp, vec_in);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+// -------------------------------------------------------------- layernorm
+// One warp per row. Mean, then the biased variance of (x - mean), as
+// csrc/kernels/layernorm.cu:44-64 does, with an IEEE 1/sqrt instead of the
+// approximate rsqrtf so results track torch's layer_norm.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// E = 768: the row lives in registers (6 float4 per lane), read once.
+__global__ void __launch_bounds__(256) layernorm768_kernel(
+    const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float* __restrict__ y, int64_t ldy, float* __restrict__ yp,
+    int64_t pld, int64_t pplane, int64_t rows, float eps) {
+  constexpr int E = 768;
+  constexpr int V = E / 128;  // float4 per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  float4 g[V], b[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    g[i] = __ldg(reinterpret_cast<const float4*>(gamma) + lane + 32 * i);
+    b[i] = __ldg(reinterpret_cast<const float4*>(beta) + lane + 32 * i);
+  }
+  for (int64_t r = warp_global; r < rows; r += nwarps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
+    float4 v[V];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      v[i] = __ldcs(xr + lane + 32 * i);
+      s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    const float mean = warp_sum(s) / static_cast<float>(E);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float a0 = v[i].x - mean, a1 = v[i].y - mean, a2 = v[i].z - mean, a3 = v[i].w - mean;
+      q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+    }
+    const float var = warp_sum(q) / static_cast<float>(E);
+    const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float4 o;
+      o.x = (v[i].x - mean) * rstd * g[i].x + b[i].x;
+      o.y = (v[i].y - mean) * rstd * g[i].y + b[i].y;
+      o.z = (v[i].z - mean) * rstd * g[i].z + b[i].z;
+      o.w = (v[i].w - mean) * rstd * g[i].w + b[i].w;
+      const int col = (lane + 32 * i) * 4;
+      if (y) *reinterpret_cast<float4*>(y + r * ldy + col) = o;
+      if (yp) {
+        float4 h, l;
+        tf32_split(o.x, h.x, l.x);
+        tf32_split(o.y, h.y, l.y);
+        tf32_split(o.z, h.z, l.z);
+        tf32_split(o.w, h.w, l.w);
+        *reinterpret_cast<float4*>(yp + r * pld + col) = h;
+        *reinterpret_cast<float4*>(yp + pplane + r * pld + col) = l;
+      }
+    }
+  }
+}
+
+// Any E: three passes over the row (the re-reads hit L1/L2).
+__global__ void layernorm_generic_kernel(const float* __restrict__ x, int64_t ldx,
+                                         const float* __restrict__ gamma,
+                                         const float* __restrict__ beta, float* __restrict__ y,
+                                         int64_t ldy, float* __restrict__ yp, int64_t pld,
+                                         int64_t pplane, int64_t rows, int E, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = warp_global; r < rows; r += nwarps) {
+    const float* xr = x + r * ldx;
+    float s = 0.f;
+    for (int c = lane; c < E; c += 32) s += xr[c];
+    const float mean = warp_sum(s) / static_cast<float>(E);
+    float q = 0.f;
+    for (int c = lane; c < E; c += 32) {
+      const float a = xr[c] - mean;
+      q += a * a;
+    }
+    const float var = warp_sum(q) / static_cast<float>(E);
+    const float rstd = 1.0f / sqrtf(var + eps);
+    for (int c = lane; c < E; c += 32) {
+      const float o = (xr[c] - mean) * rstd * gamma[c] + beta[c];
+      if (y) y[r * ldy + c] = o;
+      if (yp) {
+        float h, l;
+        tf32_split(o, h, l);
+        yp[r * pld + c] = h;
+        yp[pplane + r * pld + c] = l;
+      }
+    }
+  }
+}
+
+int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const float* beta,
+                     float* y, int64_t ldy, float* y_pair, int64_t pair_ld, int64_t pair_plane,
+                     int64_t rows, int E, float eps, cudaStream_t s) {
+  if (rows < 0 || E <= 0 || !x || !gamma || !beta || (!y && !y_pair))
+    return VITB200_E_INVALID_ARG;
+  if (rows == 0) return 0;
+  auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool fast = (E == 768) && al(x) && al(gamma) && al(beta) && (ldx % 4 == 0) &&
+                    (!y || (al(y) && ldy % 4 == 0)) &&
+                    (!y_pair || (al(y_pair) && pair_ld % 4 == 0 && pair_plane % 4 == 0));
+  const int threads = 256;
+  const int64_t work = rows * 32;
+  if (fast) {
+    layernorm768_kernel<<<grid_for(work, threads), threads, 0, s>>>(
+        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, rows, eps);
+  count_launch();
+  } else {
+    layernorm_generic_kernel<<<grid_for(work, threads), threads, 0, s>>>(
+        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, rows, E, eps);
+  count_launch();
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+// ----------------------------------------------------------------- im2col
+// img[B][C][H][W] -> pair[2][B*P][C*256], patch vector order (c, py, px) and
+// patches row-major over the (H/16) x (W/16) grid, as the reference kernel
+// csrc/kernels/patch_embed.cu:29-44 and torch's Conv2d weight layout agree.
+__global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, int H, int W,
+                                   float* __restrict__ pair) {
+  const int gw = W / 16, gh = H / 16;
+  const int P = gw * gh;
+  const int K = C * 256;
+  const int q_per_row = K / 4;
+  const int64_t rows = static_cast<int64_t>(B) * P;
+  const int64_t total = rows * q_per_row;
+  const int64_t plane = rows * K;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / q_per_row;
+    const int k = static_cast<int>(i - m * q_per_row) * 4;
+    const int64_t b = m / P;
+    const int p = static_cast<int>(m - b * P);
+    const int gy = p / gw, gx = p - (p / gw) * gw;
+    const int c = k >> 8, py = (k >> 4) & 15, px = k & 15;
+    const float* src = img + ((b * C + c) * H + gy * 16 + py) * static_cast<int64_t>(W) +
+                       gx * 16 + px;
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(src));
+    float4 h, l;
+    tf32_split(v.x, h.x, l.x);
+    tf32_split(v.y, h.y, l.y);
+    tf32_split(v.z, h.z, l.z);
+    tf32_split(v.w, h.w, l.w);
+    float* dst = pair + m * K + k;
+    *reinterpret_cast<float4*>(dst) = h;
+    *reinterpret_cast<float4*>(dst + plane) = l;
+    (void)gh;
+  }
+}
+
+int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair,
+                       cudaStream_t s) {
+  if (B < 0 || C <= 0 || H <= 0 || W <= 0 || H % 16 || W % 16 || !img || !pair)
+    return VITB200_E_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(img) % 16 || reinterpret_cast<uintptr_t>(pair) % 16)
+    return VITB200_E_ALIGNMENT;
+  if (B == 0) return 0;
+  const int64_t work = static_cast<int64_t>(B) * (H / 16) * (W / 16) * C * 64;
+  im2col_pair_kernel<<<grid_for(work, 256), 256, 0, s>>>(img, B, C, H, W, pair);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+// ------------------------------------------------------------ CLS + pos
+// out[b][0] = cls[b] + pos[0]; when patches != null also
+// out[b][1+p] = patches[b][p] + pos[1+p] (csrc/kernels/pos_encoding.cu:8-28 with
+// P a runtime value). cls_stride 0 broadcasts one CLS row to every image.
+__global__ void cls_pos_kernel(const float* __restrict__ cls, int64_t cls_stride,
+                               const float* __restrict__ pos, const float* __restrict__ patches,
+                               float* __restrict__ out, int B, int P, int E) {
+  const int T = P + 1;
+  const int64_t rows = patches ? static_cast<int64_t>(B) * T : B;
+  const int64_t total = rows * E;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / E;
+    const int n = static_cast<int>(i - r * E);
+    int64_t b, t;
+    if (patches) {
+      b = r / T;
+      t = r - b * T;
+    } else {
+      b = r;
+      t = 0;
+    }
+    const float base = (t == 0) ? cls[b * cls_stride + n] : patches[(b * P + t - 1) * E + n];
+    out[(b * T + t) * E + n] = base + pos[t * E + n];
+  }
+}
+
+int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const float* patches,
+                   float* out, int B, int P, int E, cudaStream_t s) {
+  if (B < 0 || P < 0 || E <= 0 || !cls || !pos || !out) return VITB200_E_INVALID_ARG;
+  if (B == 0) return 0;
+  const int64_t rows = patches ? static_cast<int64_t>(B) * (P + 1) : B;
+  cls_pos_kernel<<<grid_for(rows * E, 256), 256, 0, s>>>(cls, cls_stride, pos, patches, out, B,
+                                                          P, E);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+// ------------------------------------------------------------ K = 0 GEMM
+// With an empty reduction the product is 0; only the epilogue remains
+// (bias, GELU, residual), matching the reference CuTe kernel's K=0 behaviour.
+__global__ void gemm_k0_kernel(int64_t M, int N, GemmEpilogue e) {
+  const int64_t total = M * N;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / N;
+    const int n = static_cast<int>(i - m * N);
+    float v = e.bias ? e.bias[n] : 0.f;
+    if (e.gelu) v = gelu_erf(v);
+    if (e.residual) v = e.residual[m * e.ldr + n] + v;
+    if (e.out) e.out[m * e.ldo + n] = v;
+    if (e.out_pair) {
+      float h, l;
+      tf32_split(v, h, l);
+      e.out_pair[m * e.ldp + n] = h;
+      e.out_pair[e.pair_plane + m * e.ldp + n] = l;
+    }
+  }
+}
+
+int gemm_k0_launch(const GemmProblem& p, cudaStream_t s) {
+  if (p.epi.mode != kModePlain) return VITB200_E_UNSUPPORTED;
+  gemm_k0_kernel<<<grid_for(p.M * p.N, 256), 256, 0, s>>>(p.M, p.N, p.epi);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace vitb200

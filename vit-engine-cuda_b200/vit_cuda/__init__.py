@@ -1,0 +1,25 @@
+"""vit_cuda — B200-native (sm_100a) ViT-B/16 inference with the reference
+project's drop-in surface: the eight ops of ``vit_cuda._C`` re-exported as
+``vit_cuda.<op>`` (the reference tests call them that way, e.g.
+tests/test_qkv.py:37) and ``vit_cuda.model.ViTCUDA``.
+"""
+from . import _C
+from ._C import (classifier_forward, flash_attn_2, gemm_bias, layernorm_forward, mlp_forward,
+                 patch_embed, pos_encoding, qkv_proj)
+from ._lib import VitB200Error, device_error
+from .model import ViTBlockCUDA, ViTCUDA
+
+__all__ = [
+    "flash_attn_2",
+    "patch_embed",
+    "pos_encoding",
+    "mlp_forward",
+    "layernorm_forward",
+    "classifier_forward",
+    "qkv_proj",
+    "gemm_bias",
+    "ViTCUDA",
+    "ViTBlockCUDA",
+    "VitB200Error",
+    "device_error",
+]

@@ -1,0 +1,129 @@
+"""ctypes binding of libvitb200.so, the C ABI declared in include/vitb200.h.
+
+The library is the product path: there is no fallback. Importing this module
+raises ImportError when the library has not been built (run
+``python vit-engine-cuda_b200/build.py`` or ``__graft_entry__.build()``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libvitb200.so")
+
+# Status codes (include/vitb200.h).
+OK = 0
+E_INVALID_ARG = -1
+E_UNSUPPORTED = -2
+E_WORKSPACE = -3
+E_DEVICE_TIMEOUT = -4
+E_NO_TMA = -5
+E_ALIGNMENT = -6
+
+EPI_NONE = 0
+EPI_BIAS = 1
+EPI_BIAS_GELU = 2
+EPI_BIAS_RESID = 3
+
+
+class VitB200Error(RuntimeError):
+    """A libvitb200 entry point returned a non-zero status."""
+
+    def __init__(self, what: str, status: int):
+        self.status = status
+        super().__init__(f"{what}: {status_string(status)} (status {status})")
+
+
+class BlockParams(ctypes.Structure):
+    _fields_ = [(name, c_void_p) for name in (
+        "norm1_w", "norm1_b", "qkv_w_pair", "qkv_b", "proj_w_pair", "proj_b",
+        "norm2_w", "norm2_b", "fc1_w_pair", "fc1_b", "fc2_w_pair", "fc2_b")]
+
+
+class VitParams(ctypes.Structure):
+    _fields_ = [
+        ("depth", c_int), ("embed_dim", c_int), ("num_heads", c_int), ("mlp_dim", c_int),
+        ("patch", c_int), ("in_chans", c_int), ("img_h", c_int), ("img_w", c_int),
+        ("num_classes", c_int), ("ln_eps", c_float), ("attn_scale", c_float),
+        ("patch_w_pair", c_void_p), ("patch_b", c_void_p), ("cls_token", c_void_p),
+        ("pos_embed", c_void_p), ("blocks", POINTER(BlockParams)),
+        ("norm_w", c_void_p), ("norm_b", c_void_p),
+        ("head_w_pair", c_void_p), ("head_b", c_void_p),
+    ]
+
+
+_P = c_void_p
+_SIGNATURES = {
+    "vitb200_version": (c_int, []),
+    "vitb200_status_string": (c_char_p, [c_int]),
+    "vitb200_init": (c_int, []),
+    "vitb200_device_error": (c_int, [POINTER(c_int), c_int]),
+    "vitb200_num_sms": (c_int, []),
+    "vitb200_launch_count": (ctypes.c_uint64, []),
+    "vitb200_set_gemm_variant": (c_int, [c_int]),
+    "vitb200_split_tf32": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int, _P]),
+    "vitb200_layernorm": (c_int, [_P, _P, _P, _P, c_int64, c_int, c_float, _P]),
+    "vitb200_gemm_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
+    "vitb200_gemm": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "vitb200_gemm_pairs": (c_int, [_P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int, c_int,
+                                   _P]),
+    "vitb200_qkv_workspace_bytes": (c_size_t, [c_int64, c_int]),
+    "vitb200_qkv": (c_int, [_P, _P, _P, _P, c_int64, c_int, _P, c_size_t, _P]),
+    "vitb200_mlp_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
+    "vitb200_mlp": (c_int, [_P, _P, _P, _P, _P, _P, _P, c_int64, c_int, c_int, _P, c_size_t,
+                            _P]),
+    "vitb200_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int64, c_int64, c_int64,
+                                  c_int64, c_float, _P]),
+    "vitb200_patch_embed_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "vitb200_patch_embed": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P,
+                                    c_size_t, _P]),
+    "vitb200_pos_encoding": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    "vitb200_classifier_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "vitb200_classifier": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, _P, c_size_t,
+                                   _P]),
+    "vitb200_vit_workspace_bytes": (c_size_t, [POINTER(VitParams), c_int]),
+    "vitb200_vit_forward": (c_int, [POINTER(VitParams), _P, _P, c_int, _P, c_size_t, _P]),
+    "vitb200_vit_forward_features": (c_int, [POINTER(VitParams), _P, _P, c_int, _P, c_size_t,
+                                             _P]),
+    "vitb200_vit_embed": (c_int, [POINTER(VitParams), _P, _P, c_int, _P, c_size_t, _P]),
+    "vitb200_vit_block": (c_int, [POINTER(VitParams), c_int, _P, c_int, _P, c_size_t, _P]),
+    "vitb200_vit_head": (c_int, [POINTER(VitParams), _P, _P, _P, c_int, _P, c_size_t, _P]),
+}
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"vit_cuda: {LIB_PATH} is missing; build it with "
+            "`python vit-engine-cuda_b200/build.py` (there is no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (restype, argtypes) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    return lib
+
+
+lib = _load()
+
+
+def status_string(status: int) -> str:
+    return lib.vitb200_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise VitB200Error(what, status)
+
+
+def exported_names() -> list[str]:
+    return sorted(_SIGNATURES)
+
+
+def device_error(clear: bool = True) -> int:
+    """Synchronises the current device and returns (optionally clearing) its
+    error word: 0, or the code of a kernel that gave up on a bounded wait."""
+    code = c_int(0)
+    check(lib.vitb200_device_error(ctypes.byref(code), 1 if clear else 0), "vitb200_device_error")
+    return code.value

@@ -1,0 +1,302 @@
+"""ViT-B/16 inference module with the reference's surface
+(vit_cuda/model.py:18-166 of the reference project): ``ViTCUDA(num_classes,
+state_dict, pretrained)`` registers timm-named buffers, ``forward`` returns
+logits, ``capture_graph`` records the forward in a CUDA graph and later calls
+replay it.
+
+Behind that surface the forward is one call into libvitb200.so
+(``vitb200_vit_forward``), which chains the fused sm_100a kernels on the
+current stream: im2col -> patch GEMM (+bias +pos) -> 12 x [LN1 -> QKV GEMM ->
+attention -> proj GEMM (+bias +residual) -> LN2 -> fc1 GEMM (+bias +GELU) ->
+fc2 GEMM (+bias +residual)] -> LN(CLS rows) -> head GEMM. The linear weights are
+split once per device into TF32 hi/lo pairs (``prepare``); activations are
+split by the kernel that produces them.
+
+``ViTBlockCUDA.forward`` keeps the reference's op-by-op block (the ``_C`` ops)
+for callers that drive blocks themselves.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import _C, _lib
+from ._lib import BlockParams, VitParams, lib
+
+_BLOCK_KEYS = [
+    ("norm1_gamma", "norm1.weight"), ("norm1_beta", "norm1.bias"),
+    ("qkv_weight", "attn.qkv.weight"), ("qkv_bias", "attn.qkv.bias"),
+    ("proj_weight", "attn.proj.weight"), ("proj_bias", "attn.proj.bias"),
+    ("norm2_gamma", "norm2.weight"), ("norm2_beta", "norm2.bias"),
+    ("fc1_weight", "mlp.fc1.weight"), ("fc1_bias", "mlp.fc1.bias"),
+    ("fc2_weight", "mlp.fc2.weight"), ("fc2_bias", "mlp.fc2.bias"),
+]
+
+
+class ViTBlockCUDA(nn.Module):
+    """One pre-LN encoder block with timm-named buffers (reference model.py:18-60)."""
+
+    def __init__(self, state, idx):
+        super().__init__()
+        prefix = f"blocks.{idx}."
+        for attr, key in _BLOCK_KEYS:
+            self.register_buffer(attr, state[prefix + key])
+
+    def forward(self, x, scale, eps):
+        residual = x
+        x = _C.layernorm_forward(x, self.norm1_gamma, self.norm1_beta, eps)
+        q, k, v = _C.qkv_proj(x, self.qkv_weight, self.qkv_bias)
+        attn_out = _C.flash_attn_2(q, k, v, scale)
+        attn_out = _C.gemm_bias(attn_out, self.proj_weight, self.proj_bias)
+        x = residual + attn_out
+        residual = x
+        x = _C.layernorm_forward(x, self.norm2_gamma, self.norm2_beta, eps)
+        mlp_out = _C.mlp_forward(x, self.fc1_weight, self.fc1_bias, self.fc2_weight,
+                                 self.fc2_bias)[0]
+        return residual + mlp_out
+
+
+def _split_pair(w: torch.Tensor) -> torch.Tensor:
+    """TF32 pair [2][N][K] of a 2-D fp32 CUDA weight (K % 4 == 0)."""
+    w2 = w.reshape(w.shape[0], -1).contiguous()
+    n, k = w2.shape
+    if k % 4:
+        raise RuntimeError("weight inner dim must be a multiple of 4")
+    pair = torch.empty((2, n, k), dtype=torch.float32, device=w2.device)
+    _lib.check(lib.vitb200_split_tf32(w2.data_ptr(), n, k, k, pair.data_ptr(), k,
+                                      torch.cuda.current_stream().cuda_stream),
+               "vitb200_split_tf32")
+    return pair
+
+
+class ViTCUDA(nn.Module):
+    def __init__(self, num_classes=1000, state_dict=None, pretrained=True):
+        super().__init__()
+        if state_dict is None:
+            try:
+                import timm  # noqa: F401  (reference model.py:67-69)
+            except ImportError as e:  # pragma: no cover - timm is not in this image
+                raise RuntimeError(
+                    "ViTCUDA: pass state_dict= (timm, needed to fetch weights, is not "
+                    "installed); vit_cuda.weights.synthetic_state_dict() builds one") from e
+            state = timm.create_model("vit_base_patch16_224", pretrained=pretrained).state_dict()
+        else:
+            state = state_dict
+
+        self.num_classes = num_classes
+        self.scale = 1.0 / math.sqrt(64)
+        self.eps = 1e-6
+
+        self.register_buffer("patch_weight", state["patch_embed.proj.weight"])
+        self.register_buffer("patch_bias", state["patch_embed.proj.bias"])
+        cls = state["cls_token"]
+        self.register_buffer("cls_token", cls.reshape(1, -1) if cls.dim() != 2 else cls)
+        pos = state["pos_embed"]
+        self.register_buffer("pos_embed", pos.squeeze(0) if pos.dim() == 3 else pos)
+        depth = 0
+        while f"blocks.{depth}.norm1.weight" in state:
+            depth += 1
+        self.blocks = nn.ModuleList([ViTBlockCUDA(state, i) for i in range(depth)])
+        self.register_buffer("norm_gamma", state["norm.weight"])
+        self.register_buffer("norm_beta", state["norm.bias"])
+        self.register_buffer("head_weight", state["head.weight"])
+        self.register_buffer("head_bias", state["head.bias"])
+
+        T = self.pos_embed.shape[0]
+        grid = int(round(math.sqrt(T - 1)))
+        if grid * grid != T - 1:
+            raise RuntimeError("pos_embed length must be a square number of patches + 1")
+        self.img_size = (grid * 16, grid * 16)
+        self.in_chans = self.patch_weight.shape[1] if self.patch_weight.dim() == 4 else 3
+        self._prepared = None  # (key, pairs, params, blocks_array)
+        self._graph = None
+
+    # ----------------------------------------------------------- weights
+    def _source_key(self):
+        ptrs = tuple(b.data_ptr() for b in self.buffers())
+        return (self.patch_weight.device, ptrs)
+
+    def prepare(self, force: bool = False):
+        """Splits the linear weights into TF32 pairs on their device and builds
+        the C parameter block. Runs once per device / weight storage; call it
+        again with force=True after modifying weights in place."""
+        key = self._source_key()
+        if not force and self._prepared is not None and self._prepared[0] == key:
+            return self._prepared
+        if not self.patch_weight.is_cuda:
+            raise RuntimeError("ViTCUDA: move the model to a CUDA device first (.to('cuda'))")
+        for name, buf in self.named_buffers():
+            if buf.dtype != torch.float32:
+                raise RuntimeError(f"ViTCUDA: buffer {name} must be float32")
+        with torch.cuda.device(self.patch_weight.device):
+            _lib.check(lib.vitb200_init(), "vitb200_init")
+            pairs = {"patch": _split_pair(self.patch_weight), "head": _split_pair(self.head_weight)}
+            blocks = (BlockParams * len(self.blocks))()
+            keep = []
+            for i, blk in enumerate(self.blocks):
+                qkv, proj = _split_pair(blk.qkv_weight), _split_pair(blk.proj_weight)
+                fc1, fc2 = _split_pair(blk.fc1_weight), _split_pair(blk.fc2_weight)
+                keep += [qkv, proj, fc1, fc2]
+                vecs = [blk.norm1_gamma, blk.norm1_beta, blk.qkv_bias, blk.proj_bias,
+                        blk.norm2_gamma, blk.norm2_beta, blk.fc1_bias, blk.fc2_bias]
+                vecs = [v.contiguous() for v in vecs]
+                keep += vecs
+                blocks[i] = BlockParams(
+                    vecs[0].data_ptr(), vecs[1].data_ptr(), qkv.data_ptr(), vecs[2].data_ptr(),
+                    proj.data_ptr(), vecs[3].data_ptr(), vecs[4].data_ptr(), vecs[5].data_ptr(),
+                    fc1.data_ptr(), vecs[6].data_ptr(), fc2.data_ptr(), vecs[7].data_ptr())
+            vecs = {n: getattr(self, n).contiguous() for n in
+                    ("patch_bias", "cls_token", "pos_embed", "norm_gamma", "norm_beta",
+                     "head_bias")}
+            keep += list(vecs.values())
+            params = VitParams(
+                depth=len(self.blocks), embed_dim=768, num_heads=12,
+                mlp_dim=self.blocks[0].fc1_weight.shape[0], patch=16, in_chans=self.in_chans,
+                img_h=self.img_size[0], img_w=self.img_size[1], num_classes=self.num_classes,
+                ln_eps=self.eps, attn_scale=self.scale,
+                patch_w_pair=pairs["patch"].data_ptr(), patch_b=vecs["patch_bias"].data_ptr(),
+                cls_token=vecs["cls_token"].data_ptr(), pos_embed=vecs["pos_embed"].data_ptr(),
+                blocks=ctypes.cast(blocks, ctypes.POINTER(BlockParams)),
+                norm_w=vecs["norm_gamma"].data_ptr(), norm_b=vecs["norm_beta"].data_ptr(),
+                head_w_pair=pairs["head"].data_ptr(), head_b=vecs["head_bias"].data_ptr())
+            if self.head_weight.shape[0] != self.num_classes:
+                raise RuntimeError("head weight rows must equal num_classes")
+        self._prepared = (key, pairs, params, blocks, keep)
+        return self._prepared
+
+    @property
+    def params(self) -> VitParams:
+        return self.prepare()[2]
+
+    def workspace_bytes(self, batch: int) -> int:
+        return int(lib.vitb200_vit_workspace_bytes(ctypes.byref(self.params), int(batch)))
+
+    def _check_input(self, x: torch.Tensor) -> torch.Tensor:
+        if not isinstance(x, torch.Tensor) or not x.is_cuda:
+            raise RuntimeError("ViTCUDA: input must be a CUDA tensor")
+        if x.dtype != torch.float32:
+            raise RuntimeError("ViTCUDA: input must be float32")
+        if x.dim() != 4 or x.shape[1] != self.in_chans or tuple(x.shape[2:]) != self.img_size:
+            raise RuntimeError(
+                f"ViTCUDA: input must be [B, {self.in_chans}, {self.img_size[0]}, "
+                f"{self.img_size[1]}], got {list(x.shape)}")
+        if x.device != self.patch_weight.device:
+            raise RuntimeError("ViTCUDA: input and model must be on the same device")
+        return x.contiguous()
+
+    # ----------------------------------------------------------- forward
+    def forward(self, x):
+        # CUDA graph replay path (fixed input shape/address), reference model.py:93-99.
+        if self._graph is not None:
+            self._static_input.copy_(x)
+            self._graph.replay()
+            return self._static_output
+        return self._forward_impl(x)
+
+    def _run(self, fn_name: str, x: torch.Tensor, out_cols: int) -> torch.Tensor:
+        x = self._check_input(x)
+        params = self.params
+        B = x.shape[0]
+        out = torch.empty((B, out_cols), dtype=torch.float32, device=x.device)
+        nbytes = lib.vitb200_vit_workspace_bytes(ctypes.byref(params), B)
+        ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=x.device)
+        fn = getattr(lib, fn_name)
+        _lib.check(fn(ctypes.byref(params), x.data_ptr(), out.data_ptr(), B, ws.data_ptr(),
+                      ws.numel(), torch.cuda.current_stream().cuda_stream), fn_name)
+        return out
+
+    def _forward_impl(self, x):
+        return self._run("vitb200_vit_forward", x, self.num_classes)
+
+    def forward_features(self, x):
+        """CLS-token features after the final LayerNorm, [B, 768] (the features
+        the reference's evaluation scripts use)."""
+        return self._run("vitb200_vit_forward_features", x, 768)
+
+    # ------------------------------------------------- layerwise pieces
+    def embed(self, x: torch.Tensor) -> torch.Tensor:
+        """Token embeddings [B, T, 768] (patch embed + CLS + pos)."""
+        x = self._check_input(x)
+        params = self.params
+        B = x.shape[0]
+        T = self.pos_embed.shape[0]
+        out = torch.empty((B, T, 768), dtype=torch.float32, device=x.device)
+        ws = self._ws(B, x.device)
+        _lib.check(lib.vitb200_vit_embed(ctypes.byref(params), x.data_ptr(), out.data_ptr(), B,
+                                         ws.data_ptr(), ws.numel(),
+                                         torch.cuda.current_stream().cuda_stream),
+                   "vitb200_vit_embed")
+        return out
+
+    def block(self, layer: int, tokens: torch.Tensor) -> torch.Tensor:
+        """Runs encoder block `layer` of the fused path on a copy of tokens [B, T, 768]."""
+        params = self.params
+        y = tokens.detach().to(torch.float32).contiguous().clone()
+        B = y.shape[0]
+        ws = self._ws(B, y.device)
+        _lib.check(lib.vitb200_vit_block(ctypes.byref(params), int(layer), y.data_ptr(), B,
+                                         ws.data_ptr(), ws.numel(),
+                                         torch.cuda.current_stream().cuda_stream),
+                   "vitb200_vit_block")
+        return y
+
+    def head(self, tokens: torch.Tensor):
+        """(logits [B, C], features [B, 768]) from final tokens [B, T, 768]."""
+        params = self.params
+        t = tokens.contiguous()
+        B = t.shape[0]
+        logits = torch.empty((B, self.num_classes), dtype=torch.float32, device=t.device)
+        feats = torch.empty((B, 768), dtype=torch.float32, device=t.device)
+        ws = self._ws(B, t.device)
+        _lib.check(lib.vitb200_vit_head(ctypes.byref(params), t.data_ptr(), logits.data_ptr(),
+                                        feats.data_ptr(), B, ws.data_ptr(), ws.numel(),
+                                        torch.cuda.current_stream().cuda_stream),
+                   "vitb200_vit_head")
+        return logits, feats
+
+    def _ws(self, batch: int, device) -> torch.Tensor:
+        nbytes = lib.vitb200_vit_workspace_bytes(ctypes.byref(self.params), batch)
+        return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+    # ----------------------------------------------------------- graphs
+    def capture_graph(self, static_input, num_warmup=3):
+        """Capture the full forward pass as a CUDA graph (reference model.py:128-166).
+
+        `static_input` is a CUDA float32 tensor of the exact shape the graph will
+        replay; its storage is the graph's input buffer. After capture, `model(x)`
+        copies `x` into it and replays the graph."""
+        if not static_input.is_cuda:
+            raise RuntimeError("capture_graph: static_input must be a CUDA tensor")
+        if static_input.dtype != torch.float32:
+            raise RuntimeError("capture_graph: static_input must be float32")
+        if self._graph is not None:
+            raise RuntimeError("capture_graph: a graph is already captured")
+        static_input = static_input.contiguous()
+        self.eval()
+        self.prepare()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.no_grad():
+                for _ in range(num_warmup):
+                    self._forward_impl(static_input)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            with torch.no_grad():
+                self._static_output = self._forward_impl(static_input)
+        self._static_input = static_input
+        self._graph = graph
+        torch.cuda.synchronize()
+        return graph
+
+    def release_graph(self):
+        """Drops a captured graph; `forward` runs eagerly again."""
+        self._graph = None
+        self._static_input = None
+        self._static_output = None
