@@ -113,6 +113,24 @@ int vitb200_gemm(const float* X, const float* W, const float* bias,
                  int epilogue, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* Allocation-free variant of vitb200_gemm, for callers that cannot allocate
+ * device memory: a C or ctypes host program with no device allocator of its
+ * own, a host whose device memory is owned by another framework's pool, or a
+ * request path that cannot afford cudaMalloc's device-wide synchronisation.
+ * Same arguments (minus the workspace) and the same results as vitb200_gemm;
+ * the TF32 pairs of X and W live in a fixed 16 MiB array inside the library
+ * (resident on every GPU that loads it until the process exits). Limit:
+ * 2*M*Kp rounded up to 64, plus 2*N*Kp, at most 4,194,304 floats (Kp = K rounded
+ * up to 4; e.g. M = N = K = 1024); larger problems return VITB200_E_WORKSPACE
+ * without launching. Calls share that array: calls whose GPU work can overlap
+ * (unordered streams, concurrent host threads) race; calls on one stream are
+ * safe. The first call on a device looks up the array's device address; make
+ * it before any stream capture. Allocates nothing. It has no counterpart in
+ * the reference. */
+int vitb200_gemm_noalloc(const float* X, const float* W, const float* bias,
+                         const float* residual, float* Y, int64_t M, int K, int N,
+                         int epilogue, void* stream);
+
 /* GEMM core on pre-split operands: a_pair [2][M][Kp], w_pair [2][N][Kp]
  * (Kp % 4 == 0, zero padded past K). Writes fp32 Y (ldy) and/or the TF32 pair
  * of the result (y_pair, [2][M][N]) — either may be NULL, not both. */

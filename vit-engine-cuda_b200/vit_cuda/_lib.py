@@ -66,6 +66,7 @@ _SIGNATURES = {
     "vitb200_layernorm": (c_int, [_P, _P, _P, _P, c_int64, c_int, c_float, _P]),
     "vitb200_gemm_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "vitb200_gemm": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "vitb200_gemm_noalloc": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int, c_int, c_int, _P]),
     "vitb200_gemm_pairs": (c_int, [_P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int, c_int,
                                    _P]),
     "vitb200_qkv_workspace_bytes": (c_size_t, [c_int64, c_int]),
