@@ -69,6 +69,9 @@ def parse_args():
     ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-p50", action="store_true")
+    ap.add_argument("--mode", choices=["full", "roofline"], default="full",
+                    help="roofline: time only the dominant GEMM launch (for ncu captures)")
+    ap.add_argument("--batch", type=int, default=None, help="override images per GPU")
     return ap.parse_args()
 
 
@@ -415,8 +418,28 @@ def p50_bs1(state, img, dev, iters: int = 200) -> dict:
     return {"graph_ms": graph, "eager_ms": eager}
 
 
+def run_roofline_only(args):
+    """The dominant kernel alone (fc1 shape for `batch` images), a small case
+    for profilers; prints one JSON line with its CUDA-event time."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    batch, img = CONFIGS[args.config]
+    if args.batch:
+        batch = args.batch
+    M = batch * ((img // 16) ** 2 + 1)
+    ms = gemm_roofline(dev, M, 3072, 768, reps=max(1, args.steps))
+    emit({"mode": "roofline", "kernel": "gemm_tf32x3 fc1", "M": M, "N": 3072, "K": 768,
+          "kernel_ms": ms, "tf32_pipe_tflops": 3 * 2.0 * M * 3072 * 768 / (ms * 1e-3) / 1e12})
+
+
 def main():
     args = parse_args()
+    if args.mode == "roofline":
+        run_roofline_only(args)
+        return
+    if args.batch:
+        CONFIGS[args.config] = (args.batch, CONFIGS[args.config][1])
     if args.impl == "reference":
         run_reference(args)
     else:
