@@ -157,11 +157,14 @@ int vitb200_mlp(const float* X, const float* W1, const float* b1,
 
 /* Non-causal multi-head attention softmax(Q K^T * scale) V over
  * q/k/v[B][T][heads*64] (row strides ldq/ldk/ldv floats), head h in columns
- * h*64..h*64+63. Writes o[B][T][heads*64] (row stride ldo). Replaces
- * flash_attn_2_forward_cuda (csrc/kernels/attention.cu:208-226). */
+ * h*64..h*64+63, on the tensor cores in TF32x3. Writes o[B][T][heads*64] (row
+ * stride ldo, 16-byte aligned). The workspace holds the TF32 pairs of q, k, v.
+ * Replaces flash_attn_2_forward_cuda (csrc/kernels/attention.cu:208-226). */
+size_t vitb200_attention_workspace_bytes(int B, int T, int heads);
 int vitb200_attention(const float* q, const float* k, const float* v, float* o,
                       int B, int T, int heads, int64_t ldq, int64_t ldk,
-                      int64_t ldv, int64_t ldo, float scale, void* stream);
+                      int64_t ldv, int64_t ldo, float scale, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /* Patch embedding as im2col + TF32x3 GEMM: img[B][C][H][W] (16x16 patches,
  * vector order (c, py, px)), weights [E][C*256] -> out[B][P][E] (+ bias when

@@ -97,7 +97,8 @@ def test_vit_workspace_query_validates_params():
     lambda: lib.vitb200_gemm_pairs(None, None, None, None, None, 0, None, 4, 6, 4, 0, None),
     lambda: lib.vitb200_split_tf32(1, 4, 8, 8, 1, 6, None),
     lambda: lib.vitb200_layernorm(None, None, None, None, 4, 768, 1e-6, None),
-    lambda: lib.vitb200_attention(1, 1, 1, 1, 1, 10, 12, 700, 768, 768, 768, 0.125, None),
+    lambda: lib.vitb200_attention(1, 1, 1, 1, 1, 10, 12, 700, 768, 768, 768, 0.125, None, 0,
+                                  None),
     lambda: lib.vitb200_pos_encoding(None, 1, 1, 1, 1, 196, 768, None),
     lambda: lib.vitb200_patch_embed(1, 1, None, 1, 1, 3, 200, 224, 768, None, 0, None),
     lambda: lib.vitb200_classifier(1, 1, None, 1, 1, 197, 768, 10, None, 0, None),

@@ -48,6 +48,7 @@ DeviceState* device_state(int* status) {
       d.err = static_cast<int*>(p);
       d.ready = true;  // gemm_prepare_device() below reads the SM count
       st = gemm_prepare_device();
+      if (!st) st = attention_prepare_device();
       if (st) d.ready = false;
     }
     d.status = st;
@@ -385,16 +386,42 @@ int vitb200_mlp(const float* X, const float* W1, const float* b1, const float* W
 
 // ---------------------------------------------------------------- attention
 
+static size_t vt_pair_floats(int B, int T, int heads) {
+  const size_t T4 = (static_cast<size_t>(T) + 3) / 4 * 4;
+  return 2 * static_cast<size_t>(B) * heads * 64 * T4;
+}
+
+size_t vitb200_attention_workspace_bytes(int B, int T, int heads) {
+  if (B < 0 || T < 0 || heads <= 0) return 0;
+  Carve c{nullptr, 0};
+  const size_t n = 2 * static_cast<size_t>(B) * T * heads * 64;
+  c.take(n);
+  c.take(n);
+  c.take(vt_pair_floats(B, T, heads));
+  return align_up(c.off, 256);
+}
+
 int vitb200_attention(const float* q, const float* k, const float* v, float* o, int B, int T,
                       int heads, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, float scale,
-                      void* stream) {
+                      void* workspace, size_t workspace_bytes, void* stream) {
   VITB200_GUARD_BEGIN
   if (B < 0 || T < 0 || heads <= 0 || !q || !k || !v || !o) return VITB200_E_INVALID_ARG;
   const int64_t width = static_cast<int64_t>(heads) * 64;
   if (ldq < width || ldk < width || ldv < width || ldo < width) return VITB200_E_INVALID_ARG;
+  if (B == 0 || T == 0) return 0;
+  const int64_t M = static_cast<int64_t>(B) * T;
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* qp = c.take(2 * static_cast<size_t>(M) * width);
+  float* kp = c.take(2 * static_cast<size_t>(M) * width);
+  float* vtp = c.take(vt_pair_floats(B, T, heads));
+  if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
   if (int st = check_ready()) return st;
-  return attention_launch(q, k, v, ldq, ldk, ldv, o, ldo, nullptr, 0, 0, B, T, heads, scale,
-                          as_stream(stream));
+  cudaStream_t s = as_stream(stream);
+  const int w = static_cast<int>(width);
+  if (int st = split_tf32_launch(q, M, w, ldq, qp, w, s)) return st;
+  if (int st = split_tf32_launch(k, M, w, ldk, kp, w, s)) return st;
+  if (int st = split_transpose_v_launch(v, ldv, B, T, heads, vtp, s)) return st;
+  return attention_launch(qp, w, 0, kp, w, 0, vtp, o, ldo, nullptr, 0, 0, B, T, heads, scale, s);
   VITB200_GUARD_END
 }
 
@@ -524,10 +551,12 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
 
 // Workspace regions of the forward. x is the residual stream [M][768];
 // pair_a holds the im2col pair, then per block the LN1 / attention / LN2 pairs;
-// qkv [M][2304]; hpair the GELU output pair [2][M][mlp]; cls_pair the final
+// qk the TF32 pair [2][M][1536] of q|k; vt the TF32 pair of V transposed per
+// (image, head) [2][B*heads][64][T4]; hpair the GELU output pair [2][M][mlp];
+// cls_pair the final
 // LN of the CLS rows.
 struct VitBuffers {
-  float *x, *pair_a, *qkv, *hpair, *cls_pair;
+  float *x, *pair_a, *qk, *vt, *hpair, *cls_pair;
 };
 
 size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve* c,
@@ -536,7 +565,8 @@ size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve
   b->x = c->take(static_cast<size_t>(d.M) * D);
   b->pair_a = c->take(2 * std::max(static_cast<size_t>(d.M) * D,
                                    static_cast<size_t>(d.Mp) * d.Kpatch));
-  b->qkv = c->take(static_cast<size_t>(d.M) * 3 * D);
+  b->qk = c->take(2 * static_cast<size_t>(d.M) * 2 * D);
+  b->vt = c->take(vt_pair_floats(batch, d.T, p->num_heads));
   b->hpair = c->take(2 * static_cast<size_t>(d.M) * p->mlp_dim);
   b->cls_pair = c->take(2 * static_cast<size_t>(batch) * D);
   return align_up(c->off, 256);
@@ -586,12 +616,19 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
     g.N = 3 * D;
     g.Kp = D;
     g.epi.bias = w.qkv_b;
-    g.epi.out = b.qkv;
-    g.epi.ldo = 3 * D;
+    g.epi.mode = kModeQKVAttn;
+    g.epi.out_pair = b.qk;
+    g.epi.ldp = 2 * D;
+    g.epi.pair_plane = M * 2 * D;
+    g.epi.e_split = D;
+    g.epi.T = d.T;
+    g.epi.T4 = (d.T + 3) / 4 * 4;
+    g.epi.vt_pair = b.vt;
+    g.epi.vt_plane = static_cast<int64_t>(vt_pair_floats(batch, d.T, p->num_heads) / 2);
     if (int st = gemm_pairs_launch(g, s)) return st;
   }
-  if (int st = attention_launch(b.qkv, b.qkv + D, b.qkv + 2 * D, 3 * D, 3 * D, 3 * D, nullptr, 0,
-                                b.pair_a, D, plane, batch, d.T, p->num_heads, p->attn_scale, s))
+  if (int st = attention_launch(b.qk, 2 * D, 0, b.qk, 2 * D, D, b.vt, nullptr, 0, b.pair_a, D,
+                                plane, batch, d.T, p->num_heads, p->attn_scale, s))
     return st;
   {
     GemmProblem g;

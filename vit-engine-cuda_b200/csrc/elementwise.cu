@@ -274,6 +274,50 @@ int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const
   return cuda_status(cudaGetLastError());
 }
 
+// ------------------------------------------------- V transpose + split
+// v[B*T][ldv] (head h at columns h*64..h*64+63) -> vt[2][B*heads][64][T4], the
+// per-head transposed TF32 pair the attention kernel reads as its V^T operand.
+// 32x32 tiles through shared memory keep both the reads and the writes
+// coalesced. Keys T..T4-1 are left untouched (the attention's tensor map stops
+// at T and zero-fills).
+__global__ void split_transpose_v_kernel(const float* __restrict__ v, int64_t ldv, int T,
+                                         int heads, int T4, float* __restrict__ vt,
+                                         int64_t vt_plane) {
+  __shared__ float tile[32][33];
+  const int bh = blockIdx.z;
+  const int b = bh / heads, h = bh - (bh / heads) * heads;
+  const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int k = ty; k < 32; k += 8) {
+    const int t = t0 + k;
+    tile[k][tx] = (t < T) ? v[(static_cast<int64_t>(b) * T + t) * ldv + h * 64 + d0 + tx] : 0.f;
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int t = t0 + tx;
+    if (t < T) {
+      float hi, lo;
+      tf32_split(tile[tx][k], hi, lo);
+      const int64_t idx = (static_cast<int64_t>(bh) * 64 + d0 + k) * T4 + t;
+      vt[idx] = hi;
+      vt[idx + vt_plane] = lo;
+    }
+  }
+}
+
+int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int heads, float* vt_pair,
+                             cudaStream_t s) {
+  if (!v || !vt_pair || B < 0 || T < 0 || heads <= 0 || ldv < heads * 64)
+    return VITB200_E_INVALID_ARG;
+  if (B == 0 || T == 0) return 0;
+  const int T4 = (T + 3) / 4 * 4;
+  const int64_t plane = static_cast<int64_t>(B) * heads * 64 * T4;
+  dim3 grid((T + 31) / 32, 2, B * heads);
+  split_transpose_v_kernel<<<grid, dim3(32, 8), 0, s>>>(v, ldv, T, heads, T4, vt_pair, plane);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
 // ------------------------------------------------------------ K = 0 GEMM
 // With an empty reduction the product is 0; only the epilogue remains
 // (bias, GELU, residual), matching the reference CuTe kernel's K=0 behaviour.

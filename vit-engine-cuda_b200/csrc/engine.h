@@ -2,6 +2,7 @@
 // Not part of the C ABI (that is include/vitb200.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -12,6 +13,8 @@ enum EpiMode : int {
   kModePlain = 0,  // out row = m
   kModePatch = 1,  // out row = (m / P) * T + 1 + m % P, adds pos[(1 + m % P)][n]
   kModeSplit3 = 2, // column n goes to plane n / e_split, column n % e_split
+  kModeQKVAttn = 3, // q|k columns -> TF32 pair rows [2][M][2E]; v columns -> the
+                    // per-head transposed pair vt[2][B*heads][64][T4] (attention's V^T)
 };
 
 struct GemmEpilogue {
@@ -27,8 +30,11 @@ struct GemmEpilogue {
   int mode = kModePlain;
   int P = 0, T = 0;                 // kModePatch
   const float* pos = nullptr;       // kModePatch: pos[T][N]
-  int e_split = 0;                  // kModeSplit3
+  int e_split = 0;                  // kModeSplit3 / kModeQKVAttn: E
   int64_t split_plane = 0;          // kModeSplit3: elements between planes
+  float* vt_pair = nullptr;         // kModeQKVAttn: [2][B*heads][64][T4]
+  int64_t vt_plane = 0;             // kModeQKVAttn: elements between vt planes
+  int T4 = 0;                       // kModeQKVAttn: T rounded up to 4
 };
 
 struct GemmProblem {
@@ -39,6 +45,17 @@ struct GemmProblem {
   int Kp = 0;                     // % 4 == 0
   GemmEpilogue epi;
 };
+
+// Encodes a tiled fp32 TMA tensor map of `rank` dims (innermost first; strides
+// in bytes for dims 1..rank-1) with the 128-byte swizzle (64-byte if
+// swizzle128 == 0). Returns a vitb200 status code.
+int encode_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides, const uint32_t* box, int swizzle128);
+
+// Encodes a TMA tensor map (CUtensorMap, passed as void*) over a TF32 pair
+// [2][rows][Kp] with box [2][box_rows][BK] and the swizzle of a BK*4-byte row.
+int make_pair_map(CUtensorMap* map, const float* pair, int64_t rows, int Kp, int box_rows,
+                  int BK);
 
 // Launches the TF32x3 tcgen05 GEMM; returns a vitb200 status code.
 int gemm_pairs_launch(const GemmProblem& p, cudaStream_t stream);
@@ -63,10 +80,20 @@ int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const
                    float* out, int B, int P, int E, cudaStream_t s);
 int gemm_k0_launch(const GemmProblem& p, cudaStream_t s);
 
-// Attention (attention.cu).
-int attention_launch(const float* q, const float* k, const float* v, int64_t ldq, int64_t ldk,
-                     int64_t ldv, float* o, int64_t ldo, float* o_pair, int64_t pair_ld,
-                     int64_t pair_plane, int B, int T, int heads, float scale, cudaStream_t s);
+// Raises the attention kernel's shared-memory limit on the current device.
+int attention_prepare_device();
+
+// Attention (attention.cu) on TF32 pairs. q_pair / k_pair are [2][B*T][ld]
+// buffers (they may be the same buffer), head h of q at columns q_col + h*64.., of
+// k at k_col + h*64..; vt_pair is V transposed per (image, head),
+// [2][B*heads][64][T4] with T4 = T rounded up to 4.
+int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* k_pair,
+                     int64_t k_ld, int k_col, const float* vt_pair, float* o, int64_t ldo,
+                     float* o_pair, int64_t pair_ld, int64_t pair_plane, int B, int T, int heads,
+                     float scale, cudaStream_t s);
+// V[B*T][ldv] (head h at columns h*64..) -> vt pair [2][B*heads][64][T4].
+int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int heads, float* vt_pair,
+                             cudaStream_t s);
 
 // Counts one kernel launch issued by the library (process-wide).
 void count_launch();

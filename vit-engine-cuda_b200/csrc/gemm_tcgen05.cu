@@ -111,6 +111,22 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& a, int64_t m, in
     const int plane = n0 / e.e_split;  // e_split % 32 == 0: a chunk never straddles
     plane_off = static_cast<int64_t>(plane) * e.split_plane;
     col_base = n0 - plane * e.e_split;
+  } else if (e.mode == kModeQKVAttn && n0 >= 2 * e.e_split) {
+    // V columns: TF32 pair of V transposed per (image, head). Lanes of a warp
+    // hold consecutive rows, so each column's store is one coalesced line.
+    const int vc = n0 - 2 * e.e_split;
+    const int64_t bimg = m / e.T;
+    const int64_t t = m - bimg * e.T;
+    const int64_t head_row = (bimg * (e.e_split / 64) + vc / 64) * 64 + (vc & 63);
+    float* dst = e.vt_pair + head_row * e.T4 + t;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float hi, lo;
+      tf32_split(v[j], hi, lo);
+      dst[static_cast<int64_t>(j) * e.T4] = hi;
+      dst[static_cast<int64_t>(j) * e.T4 + e.vt_plane] = lo;
+    }
+    return;
   }
 
   const bool full = (n0 + 32 <= N);
@@ -426,24 +442,41 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return g_encode;
 }
 
+}  // namespace
+
+int encode_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides, const uint32_t* box, int swizzle128) {
+  auto enc = encode_fn();
+  if (enc == nullptr) return VITB200_E_NO_TMA;
+  if (rank < 1 || rank > 5) return VITB200_E_INVALID_ARG;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    bx[i] = static_cast<cuuint32_t>(box[i]);
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = static_cast<cuuint64_t>(strides[i]);
+  }
+  const CUtensorMapSwizzle sw = swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank),
+                   const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : VITB200_E_NO_TMA;
+}
+
 // Tensor map over a TF32 pair [2][rows][Kp]: box = [2][box_rows][BK] with the
 // swizzle matching a BK*4-byte row.
 int make_pair_map(CUtensorMap* map, const float* pair, int64_t rows, int Kp, int box_rows,
                   int BK) {
-  auto enc = encode_fn();
-  if (enc == nullptr) return VITB200_E_NO_TMA;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows), 2};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp) * 4,
-                           static_cast<cuuint64_t>(rows) * static_cast<cuuint64_t>(Kp) * 4};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows), 2};
-  cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapSwizzle sw =
-      (BK * 4 == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(pair), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : VITB200_E_NO_TMA;
+  const uint64_t dims[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(rows), 2};
+  const uint64_t strides[2] = {static_cast<uint64_t>(Kp) * 4,
+                               static_cast<uint64_t>(rows) * static_cast<uint64_t>(Kp) * 4};
+  const uint32_t box[3] = {static_cast<uint32_t>(BK), static_cast<uint32_t>(box_rows), 2};
+  return encode_tmap(map, 3, pair, dims, strides, box, BK * 4 == 128);
 }
+
+namespace {
 
 struct Variant {
   int bn, bk, stages, chunk_kb;
@@ -540,6 +573,11 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
   if (p.M == 0 || p.N == 0) return 0;
   if (p.epi.mode == kModeSplit3 && (p.epi.e_split <= 0 || p.epi.e_split % 32 != 0))
     return VITB200_E_UNSUPPORTED;
+  if (p.epi.mode == kModeQKVAttn &&
+      (p.epi.e_split <= 0 || p.epi.e_split % 64 != 0 || p.N != 3 * p.epi.e_split ||
+       !p.epi.vt_pair || !p.epi.out_pair || p.epi.out || p.epi.residual || p.epi.T <= 0 ||
+       p.epi.T4 < p.epi.T || p.epi.ldp != 2 * p.epi.e_split))
+    return VITB200_E_INVALID_ARG;
   if (p.epi.mode == kModePatch && (p.epi.P <= 0 || p.epi.T != p.epi.P + 1 || !p.epi.pos))
     return VITB200_E_INVALID_ARG;
   if (p.Kp == 0) return gemm_k0_launch(p, s);

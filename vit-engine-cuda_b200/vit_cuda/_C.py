@@ -82,9 +82,10 @@ def flash_attn_2(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float
     if E != 768:
         raise RuntimeError("E dimension must be 768")
     O = torch.empty_like(Qc)
+    ws = _workspace(lib.vitb200_attention_workspace_bytes(B, N, 12), Qc.device)
     _lib.check(lib.vitb200_attention(Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(),
-                                     B, N, 12, E, E, E, E, float(scale), _stream()),
-               "flash_attn_2")
+                                     B, N, 12, E, E, E, E, float(scale), ws.data_ptr(),
+                                     ws.numel(), _stream()), "flash_attn_2")
     return O
 
 

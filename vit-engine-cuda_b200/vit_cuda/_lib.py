@@ -74,8 +74,9 @@ _SIGNATURES = {
     "vitb200_mlp_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "vitb200_mlp": (c_int, [_P, _P, _P, _P, _P, _P, _P, c_int64, c_int, c_int, _P, c_size_t,
                             _P]),
+    "vitb200_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "vitb200_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int64, c_int64, c_int64,
-                                  c_int64, c_float, _P]),
+                                  c_int64, c_float, _P, c_size_t, _P]),
     "vitb200_patch_embed_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "vitb200_patch_embed": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P,
                                     c_size_t, _P]),
