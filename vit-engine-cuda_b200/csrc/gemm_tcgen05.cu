@@ -16,7 +16,7 @@
 //  * warp 1: allocates TMEM and, from one thread, issues tcgen05.mma.kind::tf32
 //    (M=128, N=BN, K=8) — lo*hi, hi*lo, hi*hi per 8-wide K slice — into four
 //    TMEM chunk accumulators (two per epilogue warpgroup); a chunk spans
-//    CHUNK_KB stages (K = 64) and
+//    CHUNK_KB stages (K = 128) and
 //    starts from zero. The tensor core's accumulator truncates toward zero, so
 //    keeping each chain short is what holds FP32-level accuracy;
 //  * warps 2-5 and 6-9: two epilogue warpgroups that take alternate tiles. The
@@ -483,7 +483,7 @@ struct Variant {
 };
 // Index 1.. are selectable with gemm_set_variant; 0 = automatic.
 constexpr Variant kVariants[] = {
-    {0, 0, 0, 0}, {128, 32, 3, 2}, {128, 16, 6, 4}, {64, 32, 4, 2},
+    {0, 0, 0, 0}, {128, 32, 3, 4}, {128, 16, 6, 8}, {64, 32, 4, 4}, {128, 32, 3, 2},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 int g_forced_variant = 0;
@@ -560,9 +560,10 @@ int gemm_set_variant(int v) {
 }
 
 int gemm_prepare_device() {
-  int st = set_smem_attr<128, 32, 3, 2>();
-  if (!st) st = set_smem_attr<128, 16, 6, 4>();
-  if (!st) st = set_smem_attr<64, 32, 4, 2>();
+  int st = set_smem_attr<128, 32, 3, 4>();
+  if (!st) st = set_smem_attr<128, 16, 6, 8>();
+  if (!st) st = set_smem_attr<64, 32, 4, 4>();
+  if (!st) st = set_smem_attr<128, 32, 3, 2>();
   if (!st && encode_fn() == nullptr) st = VITB200_E_NO_TMA;
   return st;
 }
@@ -588,9 +589,10 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
   if (err == nullptr) return VITB200_E_INVALID_ARG;
   const int v = g_forced_variant ? g_forced_variant : pick_variant(p.M, p.N);
   switch (v) {
-    case 1: return launch_variant<128, 32, 3, 2>(p, err, s);
-    case 2: return launch_variant<128, 16, 6, 4>(p, err, s);
-    case 3: return launch_variant<64, 32, 4, 2>(p, err, s);
+    case 1: return launch_variant<128, 32, 3, 4>(p, err, s);
+    case 2: return launch_variant<128, 16, 6, 8>(p, err, s);
+    case 3: return launch_variant<64, 32, 4, 4>(p, err, s);
+    case 4: return launch_variant<128, 32, 3, 2>(p, err, s);
     default: return VITB200_E_UNSUPPORTED;
   }
 }
