@@ -76,12 +76,14 @@ int vitb200_num_sms(void);
  * streams; a CUDA-graph replay issues none). For benchmarks and tests. */
 uint64_t vitb200_launch_count(void);
 
-/* GEMM tile configuration: 0 = automatic (default), 1 = 128x128 tiles with 3
- * shared-memory stages of K=32, 2 = 128x128 with 6 stages of K=16,
- * 3 = 128x64 with 4 stages of K=32 (these accumulate K in chunks of 128 on
- * the tensor core and sum chunks in FP32 registers), 4 = as 1 with chunks of
- * 64 (about half the accumulation error, about 8% slower).
- * Returns the previous setting. For tuning and tests; process-wide. */
+/* GEMM tile configuration: 0 = automatic (default); 1..8 force one of the
+ * compiled configurations: 1 = 128x128 tiles, 2 stages of K=32; 2 = 128x128,
+ * 5 stages of K=16; 3 = 128x64, 3 stages of K=32; 4 = as 1 with K chunks of 64;
+ * 5 = 128x256, 3 stages of K=16; 6 = 256x256 on a CTA pair, 2 stages of K=32;
+ * 7 = 256x256 pair, 5 stages of K=16; 8 = as 7 with K chunks of 256. All
+ * accumulate K in chunks (128 unless stated) on the tensor core and sum the
+ * chunks in FP32 registers. Returns the previous setting. For tuning and
+ * tests; process-wide. */
 int vitb200_set_gemm_variant(int variant);
 
 /* ---- TF32 split -------------------------------------------------------- */

@@ -93,7 +93,7 @@ def test_gemm_multi_tile(vlib, cuda, shape, epi):
     check_fp32_parity(y, x, w, bias, res, epi)
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6, 7, 8])
 @pytest.mark.parametrize("shape", [(394, 768, 2304), (200, 3072, 768), (130, 96, 520),
                                    (2100, 300, 1300)])
 def test_gemm_variants(vlib, cuda, variant, shape):

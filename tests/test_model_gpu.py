@@ -38,6 +38,18 @@ def test_logits_match_oracle(case224, cuda):
     assert torch.equal(out.argmax(-1), ref.argmax(-1))
 
 
+def test_batch8_matches_oracle(case224, cuda):
+    """The reference's own end-to-end batch (tests/test_end_to_end.py:22-45 uses
+    B=8); M = 8*197 rows selects the CTA-pair GEMM tiles."""
+    state, _, _, _, model = case224
+    img = synthetic_images(8, 224, seed=5)
+    ref = orc.vit_forward(img, state)
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
 def test_logits_match_golden(case224, cuda):
     """The committed transformers-generated golden logits (tests/golden)."""
     _, img, _, _, model = case224

@@ -65,6 +65,27 @@ def compile_one(src: str) -> tuple[str, str]:
     return obj, r.stderr
 
 
+# Kernels that move registers between warpgroups with setmaxnreg, and the
+# per-thread register count their split assumes (csrc/gemm_tcgen05.cu: 384
+# threads launched at 168 registers; the warpgroups then take 56 and 224). A
+# kernel compiled to any other count would make setmaxnreg.inc wait forever.
+SETMAXNREG_KERNELS = {"gemm_tf32x3_kernel": 168}
+
+
+def check_register_split(ptxas_log: str) -> None:
+    current = None
+    for line in ptxas_log.splitlines():
+        if "Compiling entry function" in line:
+            current = next((k for k in SETMAXNREG_KERNELS if k in line), None)
+        elif current and "Used" in line and "registers" in line:
+            used = int(line.split("Used")[1].split("registers")[0])
+            if used != SETMAXNREG_KERNELS[current]:
+                raise RuntimeError(
+                    f"{current} compiled to {used} registers per thread; its setmaxnreg split "
+                    f"requires exactly {SETMAXNREG_KERNELS[current]}")
+            current = None
+
+
 def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB
@@ -73,8 +94,9 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     jobs = jobs or min(len(srcs), os.cpu_count() or 4)
     with ThreadPoolExecutor(max_workers=jobs) as ex:
         results = list(ex.map(compile_one, srcs))
-    if verbose:
-        for _, log in results:
+    for _, log in results:
+        check_register_split(log)
+        if verbose:
             sys.stderr.write(log)
     objs = [o for o, _ in results]
     tmp = LIB + ".tmp"

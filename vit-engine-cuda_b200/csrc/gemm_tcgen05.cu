@@ -14,19 +14,19 @@
 //    the hi and lo planes of a [rows][BK] K-major tile (swizzled to the BK*4-byte
 //    row) into a STAGES-deep shared-memory ring (mbarrier full/empty pairs);
 //  * warp 1: allocates TMEM and, from one thread, issues tcgen05.mma.kind::tf32
-//    (M=128, N=BN, K=8) — lo*hi, hi*lo, hi*hi per 8-wide K slice — into four
-//    TMEM chunk accumulators (two per epilogue warpgroup); a chunk spans
-//    CHUNK_KB stages (K = 128) and
+//    (M=128, N=BN, K=8) — lo*hi, hi*lo, hi*hi per 8-wide K slice — into 512/BN
+//    TMEM chunk accumulators used round robin; a chunk spans CHUNK_KB stages
+//    (K = 128) and
 //    starts from zero. The tensor core's accumulator truncates toward zero, so
 //    keeping each chain short is what holds FP32-level accuracy;
-//  * warps 2-5 and 6-9: two epilogue warpgroups that take alternate tiles. The
-//    owner of a tile drains every chunk (tcgen05.ld, one output row per thread)
-//    into an FP32 running sum in registers and frees the TMEM buffer; after the
-//    last chunk it applies bias / GELU / residual / positional add and stores
-//    fp32 and/or the TF32 pair the next GEMM consumes, while the other
-//    warpgroup is already draining the next tile's chunks.
+//  * warps 4-7 and 8-11: two epilogue warpgroups, each owning half of the tile's
+//    columns. Both drain every chunk (tcgen05.ld, one output row per thread)
+//    into FP32 running sums in registers and free the TMEM buffer; after the
+//    last chunk they apply bias / GELU / residual / positional add and store
+//    fp32 and/or the TF32 pair the next GEMM consumes, while the MMA issuer
+//    already fills the free chunk buffers with the next tile.
 //
-// No cluster launch and no multicast: every CTA loads its own tiles.
+// Every CTA loads its own tiles with plain per-CTA copies (no broadcast loads).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -54,18 +54,38 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128;
-constexpr int kThreads = 320;  // 10 warps: producer, MMA, 2 x 4 epilogue
-constexpr int kChunkBufs = 4;  // TMEM chunk accumulators, two per epilogue warpgroup
+constexpr int kEpiWarps = 8;    // two epilogue warpgroups
+constexpr int kStgPitch = 36;   // floats per row of an epilogue transpose buffer
+// 12 warps: warpgroup 0 = TMA producer, MMA issuer, two idle warps; warpgroups
+// 1 and 2 = epilogue. Launched at 168 registers per thread (65536 / 384), then
+// warpgroup 0 gives registers up (kCtrlRegs) and the epilogue warpgroups take
+// them (kEpiRegs): 128 * 56 + 256 * 224 = 384 * 168. build.py checks that ptxas
+// allocated exactly 168 registers to these kernels.
+constexpr int kThreads = 384;
+constexpr uint32_t kCtrlRegs = 56;
+constexpr uint32_t kEpiRegs = 224;
+static_assert(128 * kCtrlRegs + 256 * kEpiRegs == 384 * 168, "register split");
+constexpr int kTmemAll = 512;  // TMEM columns: chunk accumulators of BN columns each
 
-template <int BN, int BK, int STAGES, int CHUNK_KB>
+template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 struct GemmCfg {
+  // PAIR: the two CTAs of a cluster share a 256 x BN tile; each holds 128 rows
+  // of A, BN/2 rows of B and 128 x BN accumulators in its own TMEM.
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;
   static constexpr int kAPlane = kBM * BK * 4;  // bytes of one A plane (hi or lo)
-  static constexpr int kBPlane = BN * BK * 4;
+  static constexpr int kBPlane = kBRows * BK * 4;
   static constexpr int kStageBytes = 2 * kAPlane + 2 * kBPlane;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024;  // + alignment slack
-  static constexpr int kTmemCols = kChunkBufs * BN;
-  static constexpr uint32_t kIdesc = make_idesc_tf32(kBM, BN);
+  // Per epilogue warp: a 32 x 32 transpose buffer (row pitch 36 floats keeps the
+  // 16-byte row writes and the transposed reads free of bank conflicts).
+  static constexpr int kStagingBytes = kEpiWarps * 32 * kStgPitch * 4;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + 1024;
+  static constexpr int kNumBufs = kTmemAll / BN;  // chunk accumulators in TMEM
+  static constexpr int kTmemCols = kTmemAll;
+  static constexpr int kHalfN = BN / 2;           // columns per epilogue warpgroup
+  static constexpr int kTileM = PAIR ? 2 * kBM : kBM;
+  static constexpr uint32_t kIdesc = make_idesc_tf32(kTileM, BN);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(!PAIR || BN % 16 == 0, "pair N");
   static_assert(BK * 4 == 128 || BK * 4 == 64, "BK row must be a 64B or 128B swizzle span");
   static_assert((kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols >= 32 && kTmemCols <= 512,
                 "TMEM columns must be a power of two in [32, 512]");
@@ -73,14 +93,21 @@ struct GemmCfg {
   static_assert(CHUNK_KB >= 1, "chunk");
 };
 
-// Epilogue of one output row segment of 32 columns, in place on v:
-// bias -> GELU -> (positional row | column split) -> residual -> fp32 / TF32-pair stores.
-// The order of additions follows the reference: residual + (acc + bias)
+// Epilogue of one 32 x 32 slab, warp-collective: lane i holds row m_base + i,
+// columns n0..n0+31, in v (accumulator in, final values out):
+// bias -> GELU -> (positional row | column split) -> residual -> fp32 / TF32-pair
+// stores. The order of additions follows the reference: residual + (acc + bias)
 // (vit_cuda/model.py:48,60) and (conv + bias) + pos (pos_encoding.cu:20-26).
-__device__ __forceinline__ void store_row_chunk(const GemmArgs& a, int64_t m, int n0,
-                                                float (&v)[32]) {
+// Row-contiguous outputs go through the warp's transpose buffer `stg`, so every
+// global access instruction covers four whole 128-byte row segments instead of
+// sixteen bytes of 32 different rows.
+__device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base, int lane, int n0,
+                                              float (&v)[32], float* stg) {
   const GemmEpilogue& e = a.epi;
   const int N = a.N;
+  const int64_t m = m_base + lane;
+  const bool row_ok = m < a.M;
+  const bool full = (n0 + 32 <= N);
 
   if (e.bias != nullptr) {
 #pragma unroll
@@ -94,26 +121,10 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& a, int64_t m, in
     for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
   }
 
-  int64_t out_row = m;
-  int64_t col_base = n0;
-  int64_t plane_off = 0;
-  if (e.mode == kModePatch) {
-    const int64_t b = m / e.P;
-    const int p = static_cast<int>(m - b * e.P);
-    out_row = b * e.T + 1 + p;
-    const float* pos_row = e.pos + static_cast<int64_t>(1 + p) * N;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = n0 + j;
-      v[j] = v[j] + ((n < N) ? __ldg(pos_row + n) : 0.f);
-    }
-  } else if (e.mode == kModeSplit3) {
-    const int plane = n0 / e.e_split;  // e_split % 32 == 0: a chunk never straddles
-    plane_off = static_cast<int64_t>(plane) * e.split_plane;
-    col_base = n0 - plane * e.e_split;
-  } else if (e.mode == kModeQKVAttn && n0 >= 2 * e.e_split) {
-    // V columns: TF32 pair of V transposed per (image, head). Lanes of a warp
-    // hold consecutive rows, so each column's store is one coalesced line.
+  if (e.mode == kModeQKVAttn && n0 >= 2 * e.e_split) {
+    // V columns: TF32 pair of V transposed per (image, head). Lanes hold
+    // consecutive rows, so each column's store is one coalesced line.
+    if (!row_ok) return;
     const int vc = n0 - 2 * e.e_split;
     const int64_t bimg = m / e.T;
     const int64_t t = m - bimg * e.T;
@@ -129,25 +140,100 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& a, int64_t m, in
     return;
   }
 
-  const bool full = (n0 + 32 <= N);
-  if (e.residual != nullptr) {
-    const float* r = e.residual + out_row * e.ldr + col_base;
-    if (full && a.vec_res) {
+  int64_t plane_off = 0;
+  int64_t col_base = n0;
+  if (e.mode == kModeSplit3) {
+    const int plane = n0 / e.e_split;  // e_split % 32 == 0: a slab never straddles
+    plane_off = static_cast<int64_t>(plane) * e.split_plane;
+    col_base = n0 - plane * e.e_split;
+  }
+
+  const bool staged = full && e.mode != kModePatch && (!e.out || a.vec_out) &&
+                      (!e.out_pair || a.vec_pair) && (!e.residual || a.vec_res);
+  if (staged) {
+    const int rsub = lane >> 3;        // row within a group of four
+    const int c4 = (lane & 7) * 4;     // this lane's float4 within a 32-column row
+    float* my_row = stg + lane * kStgPitch;
+    if (e.residual != nullptr) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = 4 * k + rsub;
+        const int64_t mr = m_base + r;
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (mr < a.M) t = *reinterpret_cast<const float4*>(e.residual + mr * e.ldr + col_base + c4);
+        *reinterpret_cast<float4*>(stg + r * kStgPitch + c4) = t;
+      }
+      __syncwarp();
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
-        const float4 t = *reinterpret_cast<const float4*>(r + j);
+        const float4 t = *reinterpret_cast<const float4*>(my_row + j);
         v[j] = t.x + v[j];
         v[j + 1] = t.y + v[j + 1];
         v[j + 2] = t.z + v[j + 2];
         v[j + 3] = t.w + v[j + 3];
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < N) v[j] = r[j] + v[j];
+      __syncwarp();
     }
+    // Writes the warp's 32 rows from the buffer: 8 instructions, 4 rows each.
+    auto flush = [&](float* base, int64_t ld) {
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = 4 * k + rsub;
+        const int64_t mr = m_base + r;
+        const float4 t = *reinterpret_cast<const float4*>(stg + r * kStgPitch + c4);
+        if (mr < a.M) *reinterpret_cast<float4*>(base + mr * ld + col_base + c4) = t;
+      }
+      __syncwarp();
+    };
+    if (e.out != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(my_row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      flush(e.out + plane_off, e.ldo);
+    }
+    if (e.out_pair != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(my_row + j) =
+            make_float4(tf32_round(v[j]), tf32_round(v[j + 1]), tf32_round(v[j + 2]),
+                        tf32_round(v[j + 3]));
+      flush(e.out_pair, e.ldp);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 l;
+        float h;
+        tf32_split(v[j], h, l.x);
+        tf32_split(v[j + 1], h, l.y);
+        tf32_split(v[j + 2], h, l.z);
+        tf32_split(v[j + 3], h, l.w);
+        *reinterpret_cast<float4*>(my_row + j) = l;
+      }
+      flush(e.out_pair + e.pair_plane, e.ldp);
+    }
+    return;
   }
 
+  // Generic path (partial slab, positional rows, unaligned outputs): per row.
+  if (!row_ok) return;
+  int64_t out_row = m;
+  if (e.mode == kModePatch) {
+    const int64_t b = m / e.P;
+    const int p = static_cast<int>(m - b * e.P);
+    out_row = b * e.T + 1 + p;
+    const float* pos_row = e.pos + static_cast<int64_t>(1 + p) * N;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      v[j] = v[j] + ((n < N) ? __ldg(pos_row + n) : 0.f);
+    }
+  }
+  if (e.residual != nullptr) {
+    const float* r = e.residual + out_row * e.ldr + col_base;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) v[j] = r[j] + v[j];
+  }
   if (e.out != nullptr) {
     float* o = e.out + plane_off + out_row * e.ldo + col_base;
     if (full && a.vec_out) {
@@ -163,40 +249,27 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& a, int64_t m, in
   if (e.out_pair != nullptr) {
     float* ph = e.out_pair + out_row * e.ldp + col_base;
     float* pl = ph + e.pair_plane;
-    if (full && a.vec_pair) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 h, l;
-        tf32_split(v[j], h.x, l.x);
-        tf32_split(v[j + 1], h.y, l.y);
-        tf32_split(v[j + 2], h.z, l.z);
-        tf32_split(v[j + 3], h.w, l.w);
-        *reinterpret_cast<float4*>(ph + j) = h;
-        *reinterpret_cast<float4*>(pl + j) = l;
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) {
+        float h, l;
+        tf32_split(v[j], h, l);
+        ph[j] = h;
+        pl[j] = l;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < N) {
-          float h, l;
-          tf32_split(v[j], h, l);
-          ph[j] = h;
-          pl[j] = l;
-        }
-    }
   }
 }
 
-// TMEM chunk buffer of chunk j of this CTA's local tile `local`. Tiles
-// alternate between the two epilogue warpgroups and each warpgroup owns two of
-// the four buffers, so every buffer's barriers are waited on, phase after
-// phase, by exactly one waiter (mbarrier parity cannot tell phase p from p+2).
+// TMEM chunk buffer of chunk j of this CTA's local tile `local`: chunks use
+// the kNumBufs buffers round robin. Both epilogue warpgroups drain every chunk
+// (each its half of the columns) and the MMA issuer refills buffers in order,
+// so every barrier is waited on phase after phase by each of its waiters.
+template <int NBUF>
 __device__ __forceinline__ void chunk_slot(int local, int j, int num_chunks, int& buf,
                                            uint32_t& use) {
-  const int group = local & 1;
-  const uint32_t seq = static_cast<uint32_t>((local >> 1) * num_chunks + j);
-  buf = 2 * group + static_cast<int>(seq & 1u);
-  use = seq >> 1;
+  const uint32_t seq = static_cast<uint32_t>(local * num_chunks + j);
+  buf = static_cast<int>(seq % NBUF);
+  use = seq / NBUF;
 }
 
 // Lane 0 waits; the verdict is broadcast so the warp stays converged for the
@@ -222,22 +295,27 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
   }
 }
 
-template <int BN, int BK, int STAGES, int CHUNK_KB>
+template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
-  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB>;
+  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t chunk_full_bar[kChunkBufs];
-  __shared__ __align__(8) uint64_t chunk_empty_bar[kChunkBufs];
+  __shared__ __align__(8) uint64_t chunk_full_bar[Cfg::kNumBufs];
+  __shared__ __align__(8) uint64_t chunk_empty_bar[Cfg::kNumBufs];
   __shared__ __align__(8) uint64_t mma_done_bar;
   __shared__ uint32_t tmem_base_slot;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = args.err;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // rank 0 issues the pair's MMAs
+  const bool leader = rank == 0;
+  // Work units: a CTA (single) or a cluster of two (pair) per output tile.
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int num_units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   // 1024-byte aligned ring base (swizzle atoms are 8 rows x 128 B).
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -248,18 +326,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int b = 0; b < kChunkBufs; ++b) {
+    for (int b = 0; b < Cfg::kNumBufs; ++b) {
       mbar_init(&chunk_full_bar[b], 1);
-      mbar_init(&chunk_empty_bar[b], 4);  // one arrival per draining warp
+      // one arrival per draining warp (8 per CTA, of both CTAs for a pair)
+      mbar_init(&chunk_empty_bar[b], PAIR ? 16 : 8);
     }
     mbar_init(&mma_done_bar, 1);
     fence_barrier_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
   }
+  if constexpr (PAIR) cluster_sync_all();  // peer barriers initialised before any remote use
   if (warp == 1) {
-    tmem_alloc(&tmem_base_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&tmem_base_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&tmem_base_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -270,6 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_kb = args.num_kb;
   const int num_chunks = args.num_chunks;
 
+  if (warp < 4) {
+  // Control warpgroup: gives registers to the epilogue warpgroups.
+  setmaxnreg_dec<kCtrlRegs>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -277,9 +365,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int64_t issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < num_tiles && ok; tile += num_units) {
         const int m_blk = tile / args.num_n_tiles;
         const int n_blk = tile - m_blk * args.num_n_tiles;
+        const int a_row = m_blk * Cfg::kTileM + static_cast<int>(rank) * kBM;
+        const int b_row = n_blk * BN + static_cast<int>(rank) * Cfg::kBRows;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kErrWaitEmpty)) {
             ok = false;
@@ -287,9 +377,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = ring + stage * Cfg::kStageBytes;
           uint8_t* sb = sa + 2 * Cfg::kAPlane;
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
-          tma_load_3d(sa, &tmap_a, &full_bar[stage], kb * BK, m_blk * kBM, 0);
-          tma_load_3d(sb, &tmap_b, &full_bar[stage], kb * BK, n_blk * BN, 0);
+          if constexpr (PAIR) {
+            // Both CTAs' copies complete on the leader's barrier, which expects
+            // the bytes of both.
+            const uint32_t full_leader = mapa_shared(smem_addr(&full_bar[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kStageBytes);
+            tma_load_3d_pair(sa, &tmap_a, full_leader, kb * BK, a_row, 0);
+            tma_load_3d_pair(sb, &tmap_b, full_leader, kb * BK, b_row, 0);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+            tma_load_3d(sa, &tmap_a, &full_bar[stage], kb * BK, a_row, 0);
+            tma_load_3d(sb, &tmap_b, &full_bar[stage], kb * BK, b_row, 0);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -297,29 +396,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // Let every copy this thread issued land before the CTA can exit.
-      for (int s = 0; s < STAGES; ++s) {
-        if (issued > s) {
-          const int64_t fills = (issued - s + STAGES - 1) / STAGES;
-          drain_wait(&full_bar[s], static_cast<uint32_t>((fills - 1) & 1), err);
+      // Let every copy issued land before the CTAs can exit (the leader's
+      // barriers count the bytes of both CTAs of a pair).
+      if (leader) {
+        for (int s = 0; s < STAGES; ++s) {
+          if (issued > s) {
+            const int64_t fills = (issued - s + STAGES - 1) / STAGES;
+            drain_wait(&full_bar[s], static_cast<uint32_t>((fills - 1) & 1), err);
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      // Arrive on a barrier of this CTA and, for a pair, on the same barrier of
+      // the peer, once the MMAs issued so far complete.
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          const uint32_t a = smem_addr(bar);
+          umma_commit_pair(a);
+          umma_commit_pair(mapa_shared(a, 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
+      for (int tile = unit; tile < num_tiles && ok; tile += num_units, ++local) {
         for (int kb = 0; kb < num_kb; ++kb) {
           const int j = kb / CHUNK_KB;
           const bool chunk_first = (kb - j * CHUNK_KB) == 0;
           const bool chunk_last = (kb - j * CHUNK_KB) == CHUNK_KB - 1 || kb == num_kb - 1;
           int buf;
           uint32_t use;
-          chunk_slot(local, j, num_chunks, buf, use);
+          chunk_slot<Cfg::kNumBufs>(local, j, num_chunks, buf, use);
           if (chunk_first) {
             if (!mbar_wait(&chunk_empty_bar[buf], (use & 1u) ^ 1u, err, kErrWaitAccEmpty)) {
               ok = false;
@@ -345,67 +458,90 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, BK * 4);
             const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, BK * 4);
             const uint32_t acc0 = (chunk_first && kk == 0) ? 0u : 1u;
-            umma_tf32(d_tmem, dal, dbh, Cfg::kIdesc, acc0);  // lo * hi
-            umma_tf32(d_tmem, dah, dbl, Cfg::kIdesc, 1u);    // hi * lo
-            umma_tf32(d_tmem, dah, dbh, Cfg::kIdesc, 1u);    // hi * hi
+            if constexpr (PAIR) {
+              umma_tf32_pair(d_tmem, dal, dbh, Cfg::kIdesc, acc0);  // lo * hi
+              umma_tf32_pair(d_tmem, dah, dbl, Cfg::kIdesc, 1u);    // hi * lo
+              umma_tf32_pair(d_tmem, dah, dbh, Cfg::kIdesc, 1u);    // hi * hi
+            } else {
+              umma_tf32(d_tmem, dal, dbh, Cfg::kIdesc, acc0);
+              umma_tf32(d_tmem, dah, dbl, Cfg::kIdesc, 1u);
+              umma_tf32(d_tmem, dah, dbh, Cfg::kIdesc, 1u);
+            }
           }
-          umma_commit(&empty_bar[stage]);  // frees the stage once these MMAs finish
+          commit(&empty_bar[stage]);  // frees the stage once these MMAs finish
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
-          if (chunk_last) umma_commit(&chunk_full_bar[buf]);
+          if (chunk_last) commit(&chunk_full_bar[buf]);
         }
       }
       // Every MMA this thread issued must finish before TMEM is released.
-      umma_commit(&mma_done_bar);
+      if constexpr (PAIR) {
+        umma_commit_pair(smem_addr(&mma_done_bar));
+      } else {
+        umma_commit(&mma_done_bar);
+      }
       drain_wait(&mma_done_bar, 0, err);
     }
+  }
   } else {
+    setmaxnreg_inc<kEpiRegs>();
     // ------------------------------------------------------------ epilogue
-    const int group = (warp - 2) >> 2;  // warpgroup 0 takes even local tiles, 1 odd
-    const int quarter = warp & 3;       // TMEM lanes [32*quarter, 32*quarter + 32)
-    const int row_in_tile = quarter * 32 + lane;
+    // Warps 4-7 and 8-11: warp w reads TMEM lanes [32*(w%4), +32) (one output
+    // row per thread); warpgroup `half` owns columns [half*BN/2, +BN/2).
+    const int half = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int col0 = half * Cfg::kHalfN;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    float* stg = reinterpret_cast<float*>(ring + STAGES * Cfg::kStageBytes) +
+                 (warp - 4) * 32 * kStgPitch;
     int local = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-      if ((local & 1) != group) continue;
+    for (int tile = unit; tile < num_tiles && ok; tile += num_units, ++local) {
       const int m_blk = tile / args.num_n_tiles;
       const int n_blk = tile - m_blk * args.num_n_tiles;
-      float sum[BN];
+      float sum[Cfg::kHalfN];
 #pragma unroll
-      for (int c = 0; c < BN; ++c) sum[c] = 0.f;
+      for (int c = 0; c < Cfg::kHalfN; ++c) sum[c] = 0.f;
       for (int j = 0; j < num_chunks; ++j) {
         int buf;
         uint32_t use;
-        chunk_slot(local, j, num_chunks, buf, use);
+        chunk_slot<Cfg::kNumBufs>(local, j, num_chunks, buf, use);
         if (!warp_wait(&chunk_full_bar[buf], use & 1u, err, kErrWaitAccFull, lane)) {
           ok = false;
           break;
         }
         tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < BN / 32; ++q) {
-          float part[32];
+        for (int q = 0; q < Cfg::kHalfN / 16; ++q) {
+          float part[16];
           __syncwarp();
-          tmem_ld_32x32b_x32(lane_base + static_cast<uint32_t>(buf * BN + q * 32), part);
+          tmem_ld_32x32b_x16(lane_base + static_cast<uint32_t>(buf * BN + col0 + q * 16), part);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) sum[q * 32 + c] += part[c];
+          for (int c = 0; c < 16; ++c) sum[q * 16 + c] += part[c];
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&chunk_empty_bar[buf]);
+        if (lane == 0) {
+          if (PAIR && !leader) {
+            mbar_arrive_cluster(mapa_shared(smem_addr(&chunk_empty_bar[buf]), 0));
+          } else {
+            mbar_arrive(&chunk_empty_bar[buf]);
+          }
+        }
       }
       if (!ok) break;
-      const int64_t m = static_cast<int64_t>(m_blk) * kBM + row_in_tile;
-      if (m < args.M) {
+      // Rows of this warp: m_base .. m_base + 31 (lane i holds row m_base + i).
+      const int64_t m_base = static_cast<int64_t>(m_blk) * Cfg::kTileM +
+                             static_cast<int64_t>(rank) * kBM + quarter * 32;
+      if (m_base < args.M) {
 #pragma unroll
-        for (int q = 0; q < BN / 32; ++q) {
-          const int n0 = n_blk * BN + q * 32;
+        for (int q = 0; q < Cfg::kHalfN / 32; ++q) {
+          const int n0 = n_blk * BN + col0 + q * 32;
           if (n0 < args.N) {
             float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[q * 32]);
-            store_row_chunk(args, m, n0, part);
+            epilogue_slab(args, m_base, lane, n0, part, stg);
           }
         }
       }
@@ -414,10 +550,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // neither CTA releases TMEM / exits early
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
   }
 }
 
@@ -479,29 +620,36 @@ int make_pair_map(CUtensorMap* map, const float* pair, int64_t rows, int Kp, int
 namespace {
 
 struct Variant {
-  int bn, bk, stages, chunk_kb;
+  int bn, bk, stages, chunk_kb, pair;
 };
 // Index 1.. are selectable with gemm_set_variant; 0 = automatic.
 constexpr Variant kVariants[] = {
-    {0, 0, 0, 0}, {128, 32, 3, 4}, {128, 16, 6, 8}, {64, 32, 4, 4}, {128, 32, 3, 2},
+    {0, 0, 0, 0, 0},    {128, 32, 2, 4, 0}, {128, 16, 5, 8, 0}, {64, 32, 3, 4, 0},
+    {128, 32, 2, 2, 0}, {256, 16, 3, 8, 0}, {256, 32, 2, 4, 1}, {256, 16, 5, 8, 1},
+    {256, 16, 5, 16, 1},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+constexpr int kPairVariant = 6;
 int g_forced_variant = 0;
 
-template <int BN, int BK, int STAGES, int CHUNK_KB>
+// Cluster-of-two slots that fit on the device at once, per device (0 = not
+// queried yet).
+int g_pair_slots[64] = {};
+
+template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
-  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB>;
+  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB, PAIR>;
   CUtensorMap ta, tb;
   int st = make_pair_map(&ta, p.a_pair, p.M, p.Kp, kBM, BK);
   if (st) return st;
-  st = make_pair_map(&tb, p.b_pair, p.N, p.Kp, BN, BK);
+  st = make_pair_map(&tb, p.b_pair, p.N, p.Kp, Cfg::kBRows, BK);
   if (st) return st;
   GemmArgs a;
   a.M = p.M;
   a.N = p.N;
   a.Kp = p.Kp;
   a.num_n_tiles = (p.N + BN - 1) / BN;
-  const int64_t m_tiles = (p.M + kBM - 1) / kBM;
+  const int64_t m_tiles = (p.M + Cfg::kTileM - 1) / Cfg::kTileM;
   const int64_t tiles = m_tiles * a.num_n_tiles;
   if (tiles > 0x7fffffff) return VITB200_E_UNSUPPORTED;
   a.num_tiles = static_cast<int>(tiles);
@@ -516,24 +664,63 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
               (e.ldr % 4 == 0);
   a.err = err;
   a.epi = e;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, device_num_sms()));
-  gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB><<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, a);
-  count_launch();
-  return cuda_status(cudaGetLastError());
+  if constexpr (PAIR) {
+    int dev = 0;
+    if (int st2 = cuda_status(cudaGetDevice(&dev))) return st2;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int slots = (dev >= 0 && dev < 64) ? g_pair_slots[dev] : 0;
+    if (slots <= 0) {
+      cfg.gridDim = dim3(2 * static_cast<unsigned>(device_num_sms() / 2));
+      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>,
+                                         &cfg) != cudaSuccess ||
+          slots <= 0) {
+        (void)cudaGetLastError();
+        slots = device_num_sms() / 2;
+      }
+      if (dev >= 0 && dev < 64) g_pair_slots[dev] = slots;
+    }
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
+    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>,
+                                        ta, tb, a));
+    count_launch();
+    if (st) return st;
+    return cuda_status(cudaGetLastError());
+  } else {
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, device_num_sms()));
+    gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>
+        <<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, a);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+  }
 }
 
-template <int BN, int BK, int STAGES, int CHUNK_KB>
+template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 int set_smem_attr() {
-  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB>;
-  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB>,
+  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB, PAIR>;
+  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           Cfg::kSmemBytes));
 }
 
-int pick_variant(int64_t M, int N) {
-  // Minimise (waves of tiles) x (tile width): per-tile time grows with BN for a
-  // fixed K, and a partial last wave costs a full one. Ties go to the wider tile.
+int pick_variant(int64_t M, int N, const GemmEpilogue& e) {
+  // Large problems: 256 x 128 tiles on CTA pairs (each SM streams half of B,
+  // so operand traffic per FLOP matches a 256-wide tile). Small ones (batch-1
+  // latency): the single-CTA tile width that minimises (waves of tiles) x
+  // (tile width); a partial last wave costs a full one.
   const int sms = device_num_sms();
+  // A GELU epilogue that also writes the TF32 pair has a long per-tile tail;
+  // 128-wide tiles hide it behind four chunk buffers.
+  if (M >= 1024) return (e.gelu && e.out_pair) ? 1 : kPairVariant;
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   int best = 1;
   int64_t best_cost = -1;
@@ -560,10 +747,14 @@ int gemm_set_variant(int v) {
 }
 
 int gemm_prepare_device() {
-  int st = set_smem_attr<128, 32, 3, 4>();
-  if (!st) st = set_smem_attr<128, 16, 6, 8>();
-  if (!st) st = set_smem_attr<64, 32, 4, 4>();
-  if (!st) st = set_smem_attr<128, 32, 3, 2>();
+  int st = set_smem_attr<128, 32, 2, 4, false>();
+  if (!st) st = set_smem_attr<128, 16, 5, 8, false>();
+  if (!st) st = set_smem_attr<64, 32, 3, 4, false>();
+  if (!st) st = set_smem_attr<128, 32, 2, 2, false>();
+  if (!st) st = set_smem_attr<256, 16, 3, 8, false>();
+  if (!st) st = set_smem_attr<256, 32, 2, 4, true>();
+  if (!st) st = set_smem_attr<256, 16, 5, 8, true>();
+  if (!st) st = set_smem_attr<256, 16, 5, 16, true>();
   if (!st && encode_fn() == nullptr) st = VITB200_E_NO_TMA;
   return st;
 }
@@ -587,12 +778,16 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
     return VITB200_E_ALIGNMENT;
   int* err = device_error_word();
   if (err == nullptr) return VITB200_E_INVALID_ARG;
-  const int v = g_forced_variant ? g_forced_variant : pick_variant(p.M, p.N);
+  const int v = g_forced_variant ? g_forced_variant : pick_variant(p.M, p.N, p.epi);
   switch (v) {
-    case 1: return launch_variant<128, 32, 3, 4>(p, err, s);
-    case 2: return launch_variant<128, 16, 6, 8>(p, err, s);
-    case 3: return launch_variant<64, 32, 4, 4>(p, err, s);
-    case 4: return launch_variant<128, 32, 3, 2>(p, err, s);
+    case 1: return launch_variant<128, 32, 2, 4, false>(p, err, s);
+    case 2: return launch_variant<128, 16, 5, 8, false>(p, err, s);
+    case 3: return launch_variant<64, 32, 3, 4, false>(p, err, s);
+    case 4: return launch_variant<128, 32, 2, 2, false>(p, err, s);
+    case 5: return launch_variant<256, 16, 3, 8, false>(p, err, s);
+    case 6: return launch_variant<256, 32, 2, 4, true>(p, err, s);
+    case 7: return launch_variant<256, 16, 5, 8, true>(p, err, s);
+    case 8: return launch_variant<256, 16, 5, 16, true>(p, err, s);
     default: return VITB200_E_UNSUPPORTED;
   }
 }
