@@ -536,13 +536,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t m_base = static_cast<int64_t>(m_blk) * Cfg::kTileM +
                              static_cast<int64_t>(rank) * kBM + quarter * 32;
       if (m_base < args.M) {
-#pragma unroll
+        // One copy of the slab code, not kHalfN/32: after each slab the sums
+        // move down by 32 registers, so the loop body indexes statically.
+#pragma unroll 1
         for (int q = 0; q < Cfg::kHalfN / 32; ++q) {
           const int n0 = n_blk * BN + col0 + q * 32;
           if (n0 < args.N) {
-            float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[q * 32]);
+            float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[0]);
             epilogue_slab(args, m_base, lane, n0, part, stg);
           }
+#pragma unroll
+          for (int c = 0; c + 32 < Cfg::kHalfN; ++c) sum[c] = sum[c + 32];
         }
       }
     }
@@ -718,9 +722,8 @@ int pick_variant(int64_t M, int N, const GemmEpilogue& e) {
   // latency): the single-CTA tile width that minimises (waves of tiles) x
   // (tile width); a partial last wave costs a full one.
   const int sms = device_num_sms();
-  // A GELU epilogue that also writes the TF32 pair has a long per-tile tail;
-  // 128-wide tiles hide it behind four chunk buffers.
-  if (M >= 1024) return (e.gelu && e.out_pair) ? 1 : kPairVariant;
+  (void)e;
+  if (M >= 1024) return kPairVariant;
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   int best = 1;
   int64_t best_cost = -1;
