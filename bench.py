@@ -15,10 +15,13 @@ line.
   e2e       the same through the public API ViTCUDA.forward with the step's
             images copied host(pinned)->device and the logits read back to pinned
             host memory inside the timed region.
-  roofline  the dominant kernel (the TF32x3 tcgen05 GEMM, fc1 shape of this
-            workload) timed with CUDA events on its stream; achieved = TF32
-            tensor-pipe FLOP/s (3 x 2MNK / t) against the dense TF32 peak of a
-            cuBLAS TF32 GEMM measured in the same run.
+  roofline  the fc1 GEMM of this workload (FP16-split operands, bias + GELU,
+            FP16-split output: the model's fc1 launch) timed alone with CUDA
+            events on its stream; achieved = FP16 tensor-pipe FLOP/s
+            (3 x 2MNK / t) against the measured dense bf16/fp16 peak
+            (MEASURED_PEAKS.json, burst: the kernel is timed alone).
+  tf32x3    the same forward with every GEMM on TF32 pairs (TF32x3), the
+            north star's formulation, for comparison.
   cpu_baseline  the CPU oracle (a PyTorch fp32 restatement of the reference
             path) on the host cores, rank 0 at N=1, on a bounded sample.
 
@@ -46,7 +49,7 @@ for _p in (PKG, REPO):
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-METRIC = "ViT-B/16 images/sec @bs256 per GPU (FP32 parity, TF32x3)"
+METRIC = "ViT-B/16 images/sec @bs256 on 1/2/4/8 B200 (FP32 parity)"
 UNIT = "images/s"
 CONFIGS = {
     # name: (images per GPU per step, image size)
@@ -157,49 +160,25 @@ def timed(fn, steps, world, dev):
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
-def cuBLAS_tf32_peak(dev) -> float:
-    """Dense TF32 TFLOP/s of a cuBLAS 8192^3 matmul, best of 10 (burst)."""
-    n = 8192
-    a = torch.randn(n, n, device=dev)
-    b = torch.randn(n, n, device=dev)
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = True
-    try:
-        for _ in range(3):
-            torch.matmul(a, b)
-        best = float("inf")
-        for _ in range(10):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            torch.matmul(a, b)
-            e1.record()
-            torch.cuda.synchronize()
-            best = min(best, e0.elapsed_time(e1))
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
-    del a, b
-    return 2 * n ** 3 / (best * 1e-3) / 1e12
-
-
 def gemm_roofline(dev, M: int, N: int, K: int, reps: int = 10):
-    """Times the TF32x3 GEMM (fc1 shape: bias + GELU, TF32-pair output) alone."""
+    """Times the fc1 GEMM as the model launches it (FP16-split operands, bias +
+    GELU, FP16-split output) alone; returns ms per launch."""
     from vit_cuda import _lib
+    from vit_cuda.split import f16_planes, f16_weight
     lib = _lib.lib
     s = torch.cuda.current_stream().cuda_stream
     a = torch.randn(M, K, device=dev)
     w = torch.randn(N, K, device=dev) * 0.02
     bias = torch.randn(N, device=dev) * 0.02
-    ap = torch.empty(2, M, K, device=dev)
-    wp = torch.empty(2, N, K, device=dev)
-    _lib.check(lib.vitb200_split_tf32(a.data_ptr(), M, K, K, ap.data_ptr(), K, s), "split")
-    _lib.check(lib.vitb200_split_tf32(w.data_ptr(), N, K, K, wp.data_ptr(), K, s), "split")
+    ap = f16_planes(a, 2)
+    wp, acc_scale = f16_weight(w)
     del a
-    out = torch.empty(2, M, N, device=dev)
+    out = torch.empty(2, M, N, dtype=torch.int16, device=dev)
 
     def launch():
-        _lib.check(lib.vitb200_gemm_pairs(ap.data_ptr(), wp.data_ptr(), bias.data_ptr(), None,
-                                          None, 0, out.data_ptr(), M, K, N, _lib.EPI_BIAS_GELU,
-                                          s), "gemm")
+        _lib.check(lib.vitb200_gemm_f16(ap.data_ptr(), wp.data_ptr(), acc_scale, bias.data_ptr(),
+                                        None, None, 0, out.data_ptr(), M, K, N,
+                                        _lib.EPI_BIAS_GELU, s), "gemm")
 
     for _ in range(3):
         launch()
@@ -213,6 +192,17 @@ def gemm_roofline(dev, M: int, N: int, K: int, reps: int = 10):
     ms = e0.elapsed_time(e1) / reps
     del ap, wp, out
     return ms
+
+
+def measured_tensor_peak():
+    """Dense bf16 (= fp16) tensor TFLOP/s from MEASURED_PEAKS.json (burst),
+    else the pool's fallback figure."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            v = float(json.load(f)["bf16_tflops"])
+        return v, "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 8192^3, burst; of measured)"
+    except (OSError, ValueError, KeyError):
+        return 1590.0, "fallback 1.59 PFLOP/s bf16 (of fallback)"
 
 
 def ncu_traffic(name: str):
@@ -302,6 +292,7 @@ def run_ours(args):
     state = synthetic_state_dict(seed=0, img_size=img)
     model = vit_cuda.ViTCUDA(state_dict={k: v.to(dev) for k, v in state.items()}).to(dev).eval()
     model.prepare()
+    operands = sorted({k for blk in model.gemm_operands for k in blk.values()})
     x_host = synthetic_images(batch, img, seed=1000 + rank)
     x_dev = x_host.to(dev)
 
@@ -333,6 +324,20 @@ def run_ours(args):
         launches = _lib.lib.vitb200_launch_count() - n0
         clk = clocks.stop()
         ms_e2e = timed(step_e2e, args.steps, world, dev)
+        # The north star's formulation: every GEMM on TF32 pairs (TF32x3).
+        model_tf32 = vit_cuda.ViTCUDA(state_dict={k: v.to(dev) for k, v in state.items()},
+                                      operands="tf32").to(dev).eval()
+        model_tf32.prepare()
+
+        def step_tf32():
+            logits = model_tf32._forward_impl(x_dev)
+            if world > 1:
+                gather_rows(logits, total)
+
+        for _ in range(args.warmup):
+            step_tf32()
+        ms_tf32 = timed(step_tf32, args.steps, world, dev)
+        del model_tf32
     assert _lib.device_error() == 0, "a kernel reported a device error"
 
     value = total * args.steps / (ms * 1e-3)
@@ -341,20 +346,20 @@ def run_ours(args):
     d2h = total * model.num_classes * 4
     del x_dev, x_in
 
-    # Roofline of the dominant kernel (TF32x3 GEMM, the fc1 launch of this workload).
+    # Roofline of the fc1 GEMM (FP16-split operands), the model's largest GEMM.
     M = batch * T
     gemm_ms = gemm_roofline(dev, M, 3072, 768)
     alg_flops = 2.0 * M * 3072 * 768
-    tf32_peak = cuBLAS_tf32_peak(dev)
+    peak, peak_src = measured_tensor_peak()
     achieved = 3 * alg_flops / (gemm_ms * 1e-3) / 1e12
-    traffic = ncu_traffic(f"gemm_tf32x3_fc1_{args.config}.json")
+    traffic = ncu_traffic(f"gemm_f16x3_fc1_{args.config}.json")
     roofline = {
-        "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-        "frac": achieved / tf32_peak, "traffic": traffic,
-        "kernel": f"gemm_tf32x3 fc1 M={M} N=3072 K=768 (+bias+GELU, TF32-pair out)",
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        "frac": achieved / peak, "traffic": traffic,
+        "kernel": f"gemm f16x3 fc1 M={M} N=3072 K=768 (+bias+GELU, FP16-split out)",
         "kernel_ms": gemm_ms, "algorithmic_tflops": alg_flops / (gemm_ms * 1e-3) / 1e12,
-        "peak_source": "cuBLAS TF32 8192^3 dense matmul measured in this run (burst); "
-                       "achieved counts the 3 TF32 products of TF32x3",
+        "peak_source": peak_src + "; achieved counts the 3 FP16 tensor products per "
+                       "algorithmic multiply-add",
     }
 
     result = {
@@ -364,11 +369,15 @@ def run_ours(args):
         "config": {"workload": args.config, "model": "ViT-B/16 (random init, seed 0)",
                    "global_batch": total, "img_size": img, "seq_len": T,
                    "parallelism": f"dp{world}" if world > 1 else "single GPU",
+                   "block_gemm_operands": "+".join(operands),
                    "l2": "inputs larger than L2 (%.0f MB per GPU per step)" % (h2d / 1e6),
                    "gflop_per_image": GFLOP_PER_IMG.get(img)},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
         "gpu_launches": int(launches),
+        "tf32x3": {"value": total * args.steps / (ms_tf32 * 1e-3), "unit": UNIT,
+                   "ms_per_step": ms_tf32 / args.steps,
+                   "note": "same forward, every GEMM on TF32 pairs (TF32x3)"},
         "roofline": roofline,
         "clocks": clk,
         "model_tflops": GFLOP_PER_IMG.get(img, 0) * value / 1e3,
@@ -429,8 +438,8 @@ def run_roofline_only(args):
         batch = args.batch
     M = batch * ((img // 16) ** 2 + 1)
     ms = gemm_roofline(dev, M, 3072, 768, reps=max(1, args.steps))
-    emit({"mode": "roofline", "kernel": "gemm_tf32x3 fc1", "M": M, "N": 3072, "K": 768,
-          "kernel_ms": ms, "tf32_pipe_tflops": 3 * 2.0 * M * 3072 * 768 / (ms * 1e-3) / 1e12})
+    emit({"mode": "roofline", "kernel": "gemm f16x3 fc1", "M": M, "N": 3072, "K": 768,
+          "kernel_ms": ms, "f16_pipe_tflops": 3 * 2.0 * M * 3072 * 768 / (ms * 1e-3) / 1e12})
 
 
 def main():

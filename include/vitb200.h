@@ -76,14 +76,17 @@ int vitb200_num_sms(void);
  * streams; a CUDA-graph replay issues none). For benchmarks and tests. */
 uint64_t vitb200_launch_count(void);
 
-/* GEMM tile configuration: 0 = automatic (default); 1..8 force one of the
- * compiled configurations: 1 = 128x128 tiles, 2 stages of K=32; 2 = 128x128,
- * 5 stages of K=16; 3 = 128x64, 3 stages of K=32; 4 = as 1 with K chunks of 64;
- * 5 = 128x256, 3 stages of K=16; 6 = 256x256 on a CTA pair, 2 stages of K=32;
- * 7 = 256x256 pair, 5 stages of K=16; 8 = as 7 with K chunks of 256. All
- * accumulate K in chunks (128 unless stated) on the tensor core and sum the
- * chunks in FP32 registers. Returns the previous setting. For tuning and
- * tests; process-wide. */
+/* GEMM tile configuration: 0 = automatic (default); 1..12 force one of the
+ * compiled configurations. On TF32 pairs: 1 = 128x128 tiles, 2 stages of K=32;
+ * 2 = 128x128, 5 stages of K=16; 3 = 128x64, 3 stages of K=32; 4 = as 1 with K
+ * chunks of 64; 5 = 128x256, 3 stages of K=16; 6 = 256x256 on a CTA pair, 2
+ * stages of K=32; 7 = 256x256 pair, 5 stages of K=16; 8 = as 7 with K chunks of
+ * 256. On FP16 splits (vitb200_gemm_f16 and the model's F16 path): 9 = 256x256
+ * pair, 2 stages of K=64; 10 = 128x128, 2 stages of K=64; 11 = 128x64, 3
+ * stages of K=64; 12 = 256x256 pair, 4 stages of K=32. A forced configuration
+ * of the other operand kind is ignored. All accumulate K in chunks (128 unless
+ * stated) on the tensor core and sum the chunks in FP32 registers. Returns the
+ * previous setting. For tuning and tests; process-wide. */
 int vitb200_set_gemm_variant(int variant);
 
 /* ---- TF32 split -------------------------------------------------------- */
@@ -140,6 +143,29 @@ int vitb200_gemm_noalloc(const float* X, const float* W, const float* bias,
 int vitb200_gemm_pairs(const float* a_pair, const float* w_pair, const float* bias,
                        const float* residual, float* Y, int64_t ldy, float* y_pair,
                        int64_t M, int Kp, int N, int epilogue, void* stream);
+
+/* FP16 split of x[rows][cols] (row stride ldx) times `scale`, written as
+ * nplanes (2 or 3) planes of planes[nplanes][rows][ldp] fp16 (ldp % 8 == 0,
+ * zero past cols): hi = fp16(x*scale), lo = fp16((x*scale - hi) * 2^11) and,
+ * with nplanes == 3, hi * 2^11 (the third plane a GEMM's W operand needs).
+ * Scaled magnitudes must stay below 32768; a larger or non-finite value sets
+ * the device error (vitb200_device_error) instead of failing silently.
+ * No reference counterpart: operand preparation of vitb200_gemm_f16. */
+int vitb200_split_f16(const float* x, int64_t rows, int cols, int64_t ldx, float scale,
+                      uint16_t* planes, int64_t ldp, int nplanes, void* stream);
+
+/* GEMM core on FP16-split operands (the three-product FP16 emulation of an
+ * FP32 GEMM): a_planes [2][M][Kp] from vitb200_split_f16 with scale 1 and
+ * nplanes 2, w_planes [3][N][Kp] from vitb200_split_f16 with scale s and
+ * nplanes 3, acc_scale = 2^-11 / s (Kp % 8 == 0, zero padded past K).
+ * Writes fp32 Y (ldy) and/or the FP16 split of the result (y_h16,
+ * [2][M][N]) — either may be NULL, not both. Accuracy matches
+ * vitb200_gemm_pairs (TF32x3); throughput is twice the TF32 rate. No
+ * reference counterpart: the reference's GEMMs are FP32 SIMT or TF32x3
+ * (csrc/kernels/gemm.cu:12-96, csrc/kernels/gemm_cute_tf32.cu:53-168). */
+int vitb200_gemm_f16(const uint16_t* a_planes, const uint16_t* w_planes, float acc_scale,
+                     const float* bias, const float* residual, float* Y, int64_t ldy,
+                     uint16_t* y_h16, int64_t M, int Kp, int N, int epilogue, void* stream);
 
 /* QKV projection: X[M][E] * W[3E][E]^T + b, written as three contiguous
  * [M][E] planes q, k, v of qkv_out[3][M][E]. Replaces qkv_kernel_launcher
@@ -207,6 +233,18 @@ typedef struct vitb200_block_params {
     const float* fc1_b;       /* [3072]                        */
     const float* fc2_w_pair;  /* TF32 pair of [768][3072]      */
     const float* fc2_b;       /* [768]                         */
+    /* Optional FP16-split weights (vitb200_split_f16 with 3 planes and scale
+     * s; acc_scale = 2^-11 / s). A GEMM whose *_w_f16 is non-NULL runs on the
+     * FP16 path (its *_w_pair may then be NULL) and the kernel producing its
+     * input writes the FP16 split instead of the TF32 pair. The caller
+     * guarantees that input's magnitudes stay below 32768 (a LayerNorm
+     * output is bounded by sqrt(E-1)*max|gamma| + max|beta|, a linear map of
+     * it by that times the weight rows' absolute sums); values beyond that
+     * set the device error. */
+    const uint16_t* qkv_w_f16;  float qkv_acc_scale;
+    const uint16_t* proj_w_f16; float proj_acc_scale;
+    const uint16_t* fc1_w_f16;  float fc1_acc_scale;
+    const uint16_t* fc2_w_f16;  float fc2_acc_scale;
 } vitb200_block_params;
 
 typedef struct vitb200_vit_params {

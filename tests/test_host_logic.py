@@ -92,3 +92,38 @@ def test_model_384_geometry():
 def test_model_requires_state_dict_without_timm():
     with pytest.raises(RuntimeError):
         vit_cuda.ViTCUDA(state_dict=None)
+
+
+def test_layernorm_bound_is_tight_and_safe():
+    """The bound used to choose FP16 operands holds for the worst-case row (one
+    outlier among equal entries reaches sqrt(E - 1)) and for random rows."""
+    import math
+    from vit_cuda.split import layernorm_bound
+    E = 768
+    g = torch.rand(E, dtype=torch.float64) * 3
+    b = torch.randn(E, dtype=torch.float64)
+    bound = layernorm_bound(g, b)
+    x = torch.zeros(4, E, dtype=torch.float64)
+    x[0, 5] = 1.0
+    x[1] = torch.randn(E, dtype=torch.float64)
+    x[2, :] = 1.0
+    x[2, 7] = -1e6
+    x[3] = torch.randn(E, dtype=torch.float64) * 1e3
+    y = torch.nn.functional.layer_norm(x, (E,), g, b, 1e-6)
+    assert float(y.abs().max()) <= bound
+    z = torch.nn.functional.layer_norm(x[:1], (E,), None, None, 0.0)
+    assert abs(float(z.abs().max()) - math.sqrt(E - 1)) < 1e-9
+
+
+def test_linear_bound_and_weight_scale():
+    import math
+    from vit_cuda.split import f16_weight_ok, f16_weight_scale, linear_bound
+    w = torch.tensor([[1.0, -2.0], [0.5, 0.25]])
+    assert linear_bound(3.0, w, torch.tensor([0.1, -0.4])) == pytest.approx(3.0 * 3.0 + 0.4)
+    for m in (1e-5, 0.02, 1.0, 7.9, 8.0, 300.0):
+        s = f16_weight_scale(torch.tensor([m, -m / 3]))
+        assert 8.0 <= m * s < 16.0 and math.log2(s) == int(math.log2(s))
+    assert f16_weight_scale(torch.zeros(3)) == 1.0
+    assert not f16_weight_ok(torch.tensor([1e-30]))
+    assert not f16_weight_ok(torch.tensor([float("inf")]))
+    assert f16_weight_ok(torch.tensor([0.02]))

@@ -133,3 +133,42 @@ def test_384_tokens577(cuda):
         out = model(img.to(cuda)).double().cpu()
     assert (out - ref).abs().max().item() <= LOGITS_ATOL
     assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
+def test_operand_choice(case224, cuda):
+    """Random-init ViT-B/16 weights bound every block GEMM input far below the
+    FP16 split's range, so all 48 run on FP16 splits by default."""
+    _, _, _, _, model = case224
+    model.prepare()
+    assert len(model.gemm_operands) == 12
+    assert all(k == "f16" for blk in model.gemm_operands for k in blk.values())
+
+
+def test_tf32_operands_match_oracle(case224, cuda):
+    state, img, ref, _, _ = case224
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()},
+                    operands="tf32").to(cuda).eval()
+    model.prepare()
+    assert all(k == "tf32" for blk in model.gemm_operands for k in blk.values())
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
+def test_out_of_range_block_falls_back_to_tf32(cuda):
+    """A LayerNorm gain large enough that the fc1 / fc2 inputs could leave the
+    FP16 split's range moves those GEMMs (only) onto TF32 pairs; results still
+    match the oracle."""
+    state = synthetic_state_dict(seed=2, img_size=224)
+    state["blocks.11.norm2.weight"] = state["blocks.11.norm2.weight"] * 3000.0
+    img = synthetic_images(2, 224, seed=2)
+    ref = orc.vit_forward(img, state)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    model.prepare()
+    assert model.gemm_operands[11] == {"qkv": "f16", "proj": "f16", "fc1": "tf32", "fc2": "tf32"}
+    assert all(k == "f16" for blk in model.gemm_operands[:11] for k in blk.values())
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))

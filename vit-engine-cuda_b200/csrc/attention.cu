@@ -57,6 +57,9 @@ struct AttnArgs {
   float* o_pair;
   int64_t pld;
   int64_t pplane;
+  uint16_t* o_h16;  // FP16 split of O (planes hi | lo * 2^11) or null
+  int64_t hld;
+  int64_t hplane;
   int* err;
 };
 
@@ -321,6 +324,23 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           *reinterpret_cast<float4*>(ph + a.pplane + c) = lv;
         }
       }
+      if (a.o_h16) {
+        uint16_t* ph = a.o_h16 + row * a.hld + h * kD;
+#pragma unroll
+        for (int c = 0; c < kD; c += 8) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            __half h0, l0, h1, l1;
+            h16_split(o[c + 2 * t] * inv, h0, l0);
+            h16_split(o[c + 2 * t + 1] * inv, h1, l1);
+            hw[t] = pack_h2(h0, h1);
+            lw[t] = pack_h2(l0, l1);
+          }
+          *reinterpret_cast<uint4*>(ph + c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(ph + a.hplane + c) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
     }
   }
 
@@ -341,8 +361,9 @@ int attention_prepare_device() {
 int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* k_pair,
                      int64_t k_ld, int k_col, const float* vt_pair, float* o, int64_t ldo,
                      float* o_pair, int64_t pair_ld, int64_t pair_plane, int B, int T, int heads,
-                     float scale, cudaStream_t s) {
-  if (B < 0 || T < 0 || heads <= 0 || !q_pair || !k_pair || !vt_pair || (!o && !o_pair))
+                     float scale, cudaStream_t s, uint16_t* o_h16, int64_t h16_ld,
+                     int64_t h16_plane) {
+  if (B < 0 || T < 0 || heads <= 0 || !q_pair || !k_pair || !vt_pair || (!o && !o_pair && !o_h16))
     return VITB200_E_INVALID_ARG;
   if (B == 0 || T == 0) return 0;
   if (heads > 65535 || B > 65535) return VITB200_E_UNSUPPORTED;
@@ -352,7 +373,8 @@ int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* 
     return VITB200_E_INVALID_ARG;
   auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   if (!al(q_pair) || !al(k_pair) || !al(vt_pair) || (o && (!al(o) || ldo % 4)) ||
-      (o_pair && (!al(o_pair) || pair_ld % 4 || pair_plane % 4)))
+      (o_pair && (!al(o_pair) || pair_ld % 4 || pair_plane % 4)) ||
+      (o_h16 && (!al(o_h16) || h16_ld % 8 || h16_plane % 8)))
     return VITB200_E_ALIGNMENT;
   CUtensorMap tq, tk, tvt;
   if (int st = make_pair_map(&tq, q_pair, M, static_cast<int>(q_ld), kQ, 32)) return st;
@@ -378,6 +400,9 @@ int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* 
   a.o_pair = o_pair;
   a.pld = pair_ld;
   a.pplane = pair_plane;
+  a.o_h16 = o_h16;
+  a.hld = h16_ld;
+  a.hplane = h16_plane;
   a.err = device_error_word();
   dim3 grid((T + kQ - 1) / kQ, heads, B);
   attention_tc_kernel<<<grid, kThreadsA, kSmem, s>>>(tq, tk, tvt, a);

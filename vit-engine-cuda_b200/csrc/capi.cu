@@ -282,6 +282,49 @@ int vitb200_gemm_pairs(const float* a_pair, const float* w_pair, const float* bi
   VITB200_GUARD_END
 }
 
+int vitb200_split_f16(const float* x, int64_t rows, int cols, int64_t ldx, float scale,
+                      uint16_t* planes, int64_t ldp, int nplanes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (rows < 0 || cols < 0 || ldp < cols || ldp % 8 != 0 || ldx < cols ||
+      (nplanes != 2 && nplanes != 3) || !(scale > 0.f))
+    return VITB200_E_INVALID_ARG;
+  if (rows > 0 && ldp > 0 && (!x || !planes)) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  return split_f16_launch(x, rows, cols, ldx, scale, planes, ldp, nplanes, as_stream(stream));
+  VITB200_GUARD_END
+}
+
+int vitb200_gemm_f16(const uint16_t* a_planes, const uint16_t* w_planes, float acc_scale,
+                     const float* bias, const float* residual, float* Y, int64_t ldy,
+                     uint16_t* y_h16, int64_t M, int Kp, int N, int epilogue, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (M < 0 || Kp < 0 || N < 0 || Kp % 8 || !(acc_scale > 0.f)) return VITB200_E_INVALID_ARG;
+  if (epilogue < VITB200_EPI_NONE || epilogue > VITB200_EPI_BIAS_RESID) return VITB200_E_INVALID_ARG;
+  if (M == 0 || N == 0) return 0;
+  GemmEpilogue e;
+  if (int st = epilogue_from_code(epilogue, bias, residual, &e)) return st;
+  if (!Y && !y_h16) return VITB200_E_INVALID_ARG;
+  if (Y && ldy < N) return VITB200_E_INVALID_ARG;
+  if (int st = check_ready()) return st;
+  GemmProblem p;
+  p.f16 = 1;
+  p.a_h16 = a_planes;
+  p.b_h16 = w_planes;
+  p.acc_scale = acc_scale;
+  p.M = M;
+  p.N = N;
+  p.Kp = Kp;
+  e.ldr = N;
+  e.out = Y;
+  e.ldo = ldy;
+  e.out_h16 = y_h16;
+  e.ldh = N;
+  e.h16_plane = M * static_cast<int64_t>(N);
+  p.epi = e;
+  return gemm_pairs_launch(p, as_stream(stream));
+  VITB200_GUARD_END
+}
+
 // ---------------------------------------------------------------- QKV
 
 size_t vitb200_qkv_workspace_bytes(int64_t M, int E) {
@@ -537,8 +580,14 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
     return VITB200_E_INVALID_ARG;
   for (int i = 0; i < p->depth; ++i) {
     const vitb200_block_params& b = p->blocks[i];
-    if (!b.norm1_w || !b.norm1_b || !b.qkv_w_pair || !b.qkv_b || !b.proj_w_pair || !b.proj_b ||
-        !b.norm2_w || !b.norm2_b || !b.fc1_w_pair || !b.fc1_b || !b.fc2_w_pair || !b.fc2_b)
+    if (!b.norm1_w || !b.norm1_b || !b.qkv_b || !b.proj_b || !b.norm2_w || !b.norm2_b ||
+        !b.fc1_b || !b.fc2_b)
+      return VITB200_E_INVALID_ARG;
+    if ((!b.qkv_w_pair && !b.qkv_w_f16) || (!b.proj_w_pair && !b.proj_w_f16) ||
+        (!b.fc1_w_pair && !b.fc1_w_f16) || (!b.fc2_w_pair && !b.fc2_w_f16))
+      return VITB200_E_INVALID_ARG;
+    if ((b.qkv_w_f16 && !(b.qkv_acc_scale > 0.f)) || (b.proj_w_f16 && !(b.proj_acc_scale > 0.f)) ||
+        (b.fc1_w_f16 && !(b.fc1_acc_scale > 0.f)) || (b.fc2_w_f16 && !(b.fc2_acc_scale > 0.f)))
       return VITB200_E_INVALID_ARG;
   }
   d->P = (p->img_h / 16) * (p->img_w / 16);
@@ -550,10 +599,11 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
 }
 
 // Workspace regions of the forward. x is the residual stream [M][768];
-// pair_a holds the im2col pair, then per block the LN1 / attention / LN2 pairs;
-// qk the TF32 pair [2][M][1536] of q|k; vt the TF32 pair of V transposed per
-// (image, head) [2][B*heads][64][T4]; hpair the GELU output pair [2][M][mlp];
-// cls_pair the final
+// pair_a holds the im2col pair, then per block the LN1 / attention / LN2
+// outputs (a TF32 pair, or an FP16 split in the same space when the consuming
+// GEMM runs on FP16 operands); qk the TF32 pair [2][M][1536] of q|k; vt the
+// TF32 pair of V transposed per (image, head) [2][B*heads][64][T4]; hpair the
+// GELU output (TF32 pair [2][M][mlp] or its FP16 split); cls_pair the final
 // LN of the CLS rows.
 struct VitBuffers {
   float *x, *pair_a, *qk, *vt, *hpair, *cls_pair;
@@ -604,14 +654,32 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
   const int D = p->embed_dim;
   const int64_t M = d.M;
   const int64_t plane = M * D;
+  const int64_t hplane = M * p->mlp_dim;
   const vitb200_block_params& w = p->blocks[layer];
-  if (int st = layernorm_launch(x, D, w.norm1_w, w.norm1_b, nullptr, 0, b.pair_a, D, plane, M, D,
-                                p->ln_eps, s))
+  // The same space holds either operand form of a GEMM input.
+  uint16_t* a16 = reinterpret_cast<uint16_t*>(b.pair_a);
+  uint16_t* h16 = reinterpret_cast<uint16_t*>(b.hpair);
+  const bool f_qkv = w.qkv_w_f16 != nullptr, f_proj = w.proj_w_f16 != nullptr;
+  const bool f_fc1 = w.fc1_w_f16 != nullptr, f_fc2 = w.fc2_w_f16 != nullptr;
+  // GEMM input A: the TF32 pair or the FP16 split in `pair`.
+  auto set_a = [](GemmProblem& g, bool f16, float* pair, const float* w_pair,
+                  const uint16_t* w_f16, float acc_scale) {
+    if (f16) {
+      g.f16 = 1;
+      g.a_h16 = reinterpret_cast<const uint16_t*>(pair);
+      g.b_h16 = w_f16;
+      g.acc_scale = acc_scale;
+    } else {
+      g.a_pair = pair;
+      g.b_pair = w_pair;
+    }
+  };
+  if (int st = layernorm_launch(x, D, w.norm1_w, w.norm1_b, nullptr, 0, f_qkv ? nullptr : b.pair_a,
+                                D, plane, M, D, p->ln_eps, s, f_qkv ? a16 : nullptr, D, plane))
     return st;
   {
     GemmProblem g;
-    g.a_pair = b.pair_a;
-    g.b_pair = w.qkv_w_pair;
+    set_a(g, f_qkv, b.pair_a, w.qkv_w_pair, w.qkv_w_f16, w.qkv_acc_scale);
     g.M = M;
     g.N = 3 * D;
     g.Kp = D;
@@ -627,13 +695,13 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
     g.epi.vt_plane = static_cast<int64_t>(vt_pair_floats(batch, d.T, p->num_heads) / 2);
     if (int st = gemm_pairs_launch(g, s)) return st;
   }
-  if (int st = attention_launch(b.qk, 2 * D, 0, b.qk, 2 * D, D, b.vt, nullptr, 0, b.pair_a, D,
-                                plane, batch, d.T, p->num_heads, p->attn_scale, s))
+  if (int st = attention_launch(b.qk, 2 * D, 0, b.qk, 2 * D, D, b.vt, nullptr, 0,
+                                f_proj ? nullptr : b.pair_a, D, plane, batch, d.T, p->num_heads,
+                                p->attn_scale, s, f_proj ? a16 : nullptr, D, plane))
     return st;
   {
     GemmProblem g;
-    g.a_pair = b.pair_a;
-    g.b_pair = w.proj_w_pair;
+    set_a(g, f_proj, b.pair_a, w.proj_w_pair, w.proj_w_f16, w.proj_acc_scale);
     g.M = M;
     g.N = D;
     g.Kp = D;
@@ -644,26 +712,30 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
     g.epi.ldo = D;
     if (int st = gemm_pairs_launch(g, s)) return st;
   }
-  if (int st = layernorm_launch(x, D, w.norm2_w, w.norm2_b, nullptr, 0, b.pair_a, D, plane, M, D,
-                                p->ln_eps, s))
+  if (int st = layernorm_launch(x, D, w.norm2_w, w.norm2_b, nullptr, 0, f_fc1 ? nullptr : b.pair_a,
+                                D, plane, M, D, p->ln_eps, s, f_fc1 ? a16 : nullptr, D, plane))
     return st;
   {
     GemmProblem g;
-    g.a_pair = b.pair_a;
-    g.b_pair = w.fc1_w_pair;
+    set_a(g, f_fc1, b.pair_a, w.fc1_w_pair, w.fc1_w_f16, w.fc1_acc_scale);
     g.M = M;
     g.N = p->mlp_dim;
     g.Kp = D;
     g.epi.bias = w.fc1_b;
     g.epi.gelu = 1;
-    g.epi.out_pair = b.hpair;
-    g.epi.ldp = p->mlp_dim;
-    g.epi.pair_plane = M * p->mlp_dim;
+    if (f_fc2) {
+      g.epi.out_h16 = h16;
+      g.epi.ldh = p->mlp_dim;
+      g.epi.h16_plane = hplane;
+    } else {
+      g.epi.out_pair = b.hpair;
+      g.epi.ldp = p->mlp_dim;
+      g.epi.pair_plane = hplane;
+    }
     if (int st = gemm_pairs_launch(g, s)) return st;
   }
   GemmProblem g;
-  g.a_pair = b.hpair;
-  g.b_pair = w.fc2_w_pair;
+  set_a(g, f_fc2, b.hpair, w.fc2_w_pair, w.fc2_w_f16, w.fc2_acc_scale);
   g.M = M;
   g.N = D;
   g.Kp = p->mlp_dim;

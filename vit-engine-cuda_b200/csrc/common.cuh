@@ -7,6 +7,7 @@
 // producer or consumer ends instead of hanging the GPU.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -20,6 +21,7 @@ enum DeviceError : int {
   kErrWaitAccFull = 3,  // epilogue waited too long for an accumulator
   kErrWaitAccEmpty = 4, // MMA issuer waited too long for a drained accumulator
   kErrDrain = 5,        // error path: in-flight copies did not land in time
+  kErrF16Range = 6,     // a value outside the FP16-split range reached a split
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 1000000000ull;  // 1 s
@@ -51,6 +53,31 @@ __device__ __forceinline__ float tf32_round(float x) {
 __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
   hi = tf32_round(x);
   lo = tf32_round(__fsub_rn(x, hi));
+}
+
+// ---- FP16 split (Ootomo & Yokota, "Recovering single precision accuracy
+// from Tensor Cores while surpassing the FP32 theoretical peak performance",
+// IJHPCA 2022) ----------------------------------------------------------
+// x ~= hi + lo * 2^-11 with hi = fp16(x) and lo = fp16((x - hi) * 2^11). The
+// remainder r = x - hi is exact in fp32 and |r| <= 2^-11 |x|; scaling it by
+// 2^11 before rounding keeps lo's 11 bits unless r is tiny, so
+// |x - hi - lo * 2^-11| <= 2^-22 |x| + 2^-36. A GEMM then needs
+// hi*hi*2^11 + hi*lo + lo*hi, which
+// the tensor core takes as three f16 products into one FP32 accumulator when
+// the B operand carries a third plane hi*2^11 (every product scaled by 2^11).
+// Finite only for |x| < 65504; kH16Limit is the bound callers keep to.
+constexpr float kH16LoScale = 2048.f;
+constexpr float kH16Limit = 32768.f;
+
+__device__ __forceinline__ void h16_split(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(__fmul_rn(__fsub_rn(x, __half2float(hi)), kH16LoScale));
+}
+
+// Two halves packed little-endian (column c in the low half, c+1 in the high).
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+  return static_cast<uint32_t>(__half_as_ushort(a)) |
+         (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
 }
 
 // Exact (erf) GELU, the activation of timm's ViT MLP.
@@ -173,6 +200,17 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (both operands f16), one CTA.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives on `bar` once every tcgen05.mma issued so far by this thread is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -233,6 +271,12 @@ __device__ __forceinline__ void setmaxnreg_inc() {
 __host__ __device__ constexpr uint32_t make_idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t(N) >> 3) << 17) |
          ((uint32_t(M) >> 4) << 24);
+}
+
+// kind::f16 instruction descriptor: FP32 accumulator, A and B both f16
+// (format 0), both K-major, no negation or sparsity.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t(N) >> 3) << 17) | ((uint32_t(M) >> 4) << 24);
 }
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with the
@@ -354,6 +398,17 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a_desc,
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f16 on a CTA pair (A rows split across the two CTAs, B columns too).
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

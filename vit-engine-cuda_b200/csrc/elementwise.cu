@@ -63,6 +63,63 @@ int split_tf32_launch(const float* x, int64_t rows, int cols, int64_t ldx, float
   return cuda_status(cudaGetLastError());
 }
 
+// x[rows][cols] * scale -> FP16 split planes out[nplanes][rows][ldo]: hi,
+// lo * 2^11 and (nplanes == 3) hi * 2^11; zero past cols. Eight columns per
+// thread (one 16-byte store per plane).
+__global__ void split_f16_kernel(const float* __restrict__ x, int64_t rows, int cols, int64_t ldx,
+                                 float scale, uint16_t* __restrict__ out, int64_t ldo,
+                                 int nplanes, int* err) {
+  const int64_t o_per_row = ldo / 8;
+  const int64_t total = rows * o_per_row;
+  const int64_t plane = rows * ldo;
+  bool bad = false;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / o_per_row;
+    const int c0 = static_cast<int>(i - r * o_per_row) * 8;
+    const float* src = x + r * ldx + c0;
+    uint32_t hw[4], lw[4], sw[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      __half h[2], l[2], s[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = c0 + 2 * t + u;
+        const float v = (c < cols) ? __fmul_rn(src[2 * t + u], scale) : 0.f;
+        bad |= !(fabsf(v) < kH16Limit);
+        h16_split(v, h[u], l[u]);
+        s[u] = __float2half_rn(__fmul_rn(__half2float(h[u]), kH16LoScale));
+      }
+      hw[t] = pack_h2(h[0], h[1]);
+      lw[t] = pack_h2(l[0], l[1]);
+      sw[t] = pack_h2(s[0], s[1]);
+    }
+    uint16_t* dst = out + r * ldo + c0;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(dst + plane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    if (nplanes == 3)
+      *reinterpret_cast<uint4*>(dst + 2 * plane) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+  }
+  if (bad) report_error(err, kErrF16Range);
+}
+
+int split_f16_launch(const float* x, int64_t rows, int cols, int64_t ldx, float scale,
+                     uint16_t* out, int64_t ldo, int nplanes, cudaStream_t s) {
+  if (rows < 0 || cols < 0 || ldo < cols || ldo % 8 != 0 || ldx < cols ||
+      (nplanes != 2 && nplanes != 3) || !(scale > 0.f))
+    return VITB200_E_INVALID_ARG;
+  if (rows == 0 || ldo == 0) return 0;
+  if (!x || !out) return VITB200_E_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(out) % 16) return VITB200_E_ALIGNMENT;
+  int* err = device_error_word();
+  if (err == nullptr) return VITB200_E_INVALID_ARG;
+  const int64_t work = rows * (ldo / 8);
+  split_f16_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, rows, cols, ldx, scale, out, ldo,
+                                                         nplanes, err);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
 // -------------------------------------------------------------- layernorm
 // One warp per row. Mean, then the biased variance of (x - mean), as
 // csrc/kernels/layernorm.cu:44-64 does, with an IEEE 1/sqrt instead of the
@@ -77,7 +134,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void __launch_bounds__(256) layernorm768_kernel(
     const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma,
     const float* __restrict__ beta, float* __restrict__ y, int64_t ldy, float* __restrict__ yp,
-    int64_t pld, int64_t pplane, int64_t rows, float eps) {
+    int64_t pld, int64_t pplane, uint16_t* __restrict__ yh, int64_t hld, int64_t hplane,
+    int64_t rows, float eps) {
   constexpr int E = 768;
   constexpr int V = E / 128;  // float4 per lane
   const int lane = threadIdx.x & 31;
@@ -125,6 +183,16 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
         *reinterpret_cast<float4*>(yp + r * pld + col) = h;
         *reinterpret_cast<float4*>(yp + pplane + r * pld + col) = l;
       }
+      if (yh) {
+        __half h0, h1, h2, h3, l0, l1, l2, l3;
+        h16_split(o.x, h0, l0);
+        h16_split(o.y, h1, l1);
+        h16_split(o.z, h2, l2);
+        h16_split(o.w, h3, l3);
+        *reinterpret_cast<uint2*>(yh + r * hld + col) = make_uint2(pack_h2(h0, h1), pack_h2(h2, h3));
+        *reinterpret_cast<uint2*>(yh + hplane + r * hld + col) =
+            make_uint2(pack_h2(l0, l1), pack_h2(l2, l3));
+      }
     }
   }
 }
@@ -134,7 +202,8 @@ __global__ void layernorm_generic_kernel(const float* __restrict__ x, int64_t ld
                                          const float* __restrict__ gamma,
                                          const float* __restrict__ beta, float* __restrict__ y,
                                          int64_t ldy, float* __restrict__ yp, int64_t pld,
-                                         int64_t pplane, int64_t rows, int E, float eps) {
+                                         int64_t pplane, uint16_t* __restrict__ yh, int64_t hld,
+                                         int64_t hplane, int64_t rows, int E, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -159,29 +228,40 @@ __global__ void layernorm_generic_kernel(const float* __restrict__ x, int64_t ld
         yp[r * pld + c] = h;
         yp[pplane + r * pld + c] = l;
       }
+      if (yh) {
+        __half h, l;
+        h16_split(o, h, l);
+        yh[r * hld + c] = __half_as_ushort(h);
+        yh[hplane + r * hld + c] = __half_as_ushort(l);
+      }
     }
   }
 }
 
 int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const float* beta,
                      float* y, int64_t ldy, float* y_pair, int64_t pair_ld, int64_t pair_plane,
-                     int64_t rows, int E, float eps, cudaStream_t s) {
-  if (rows < 0 || E <= 0 || !x || !gamma || !beta || (!y && !y_pair))
+                     int64_t rows, int E, float eps, cudaStream_t s, uint16_t* y_h16,
+                     int64_t h16_ld, int64_t h16_plane) {
+  if (rows < 0 || E <= 0 || !x || !gamma || !beta || (!y && !y_pair && !y_h16))
     return VITB200_E_INVALID_ARG;
   if (rows == 0) return 0;
   auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool fast = (E == 768) && al(x) && al(gamma) && al(beta) && (ldx % 4 == 0) &&
                     (!y || (al(y) && ldy % 4 == 0)) &&
-                    (!y_pair || (al(y_pair) && pair_ld % 4 == 0 && pair_plane % 4 == 0));
+                    (!y_pair || (al(y_pair) && pair_ld % 4 == 0 && pair_plane % 4 == 0)) &&
+                    (!y_h16 || (reinterpret_cast<uintptr_t>(y_h16) % 8 == 0 && h16_ld % 4 == 0 &&
+                                h16_plane % 4 == 0));
   const int threads = 256;
   const int64_t work = rows * 32;
   if (fast) {
     layernorm768_kernel<<<grid_for(work, threads), threads, 0, s>>>(
-        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, rows, eps);
+        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, y_h16, h16_ld, h16_plane, rows,
+        eps);
   count_launch();
   } else {
     layernorm_generic_kernel<<<grid_for(work, threads), threads, 0, s>>>(
-        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, rows, E, eps);
+        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, y_h16, h16_ld, h16_plane, rows,
+        E, eps);
   count_launch();
   }
   return cuda_status(cudaGetLastError());
@@ -336,6 +416,12 @@ __global__ void gemm_k0_kernel(int64_t M, int N, GemmEpilogue e) {
       tf32_split(v, h, l);
       e.out_pair[m * e.ldp + n] = h;
       e.out_pair[e.pair_plane + m * e.ldp + n] = l;
+    }
+    if (e.out_h16) {
+      __half h, l;
+      h16_split(v, h, l);
+      e.out_h16[m * e.ldh + n] = __half_as_ushort(h);
+      e.out_h16[e.h16_plane + m * e.ldh + n] = __half_as_ushort(l);
     }
   }
 }

@@ -35,14 +35,21 @@ struct GemmEpilogue {
   float* vt_pair = nullptr;         // kModeQKVAttn: [2][B*heads][64][T4]
   int64_t vt_plane = 0;             // kModeQKVAttn: elements between vt planes
   int T4 = 0;                       // kModeQKVAttn: T rounded up to 4
+  uint16_t* out_h16 = nullptr;      // FP16 split of the result, planes hi | lo, or null
+  int64_t ldh = 0;                  // FP16-split row stride (% 8 == 0 for 16-byte rows)
+  int64_t h16_plane = 0;            // elements between the hi and lo planes
 };
 
 struct GemmProblem {
-  const float* a_pair = nullptr;  // [2][M][Kp]
-  const float* b_pair = nullptr;  // [2][N][Kp]
+  const float* a_pair = nullptr;  // TF32: [2][M][Kp]
+  const float* b_pair = nullptr;  // TF32: [2][N][Kp]
+  int f16 = 0;                    // 1: FP16-split operands below instead
+  const uint16_t* a_h16 = nullptr;  // F16: [2][M][Kp] planes hi, lo (lo scaled by 2^11)
+  const uint16_t* b_h16 = nullptr;  // F16: [3][N][Kp] planes hi, lo * 2^11, hi * 2^11
+  float acc_scale = 1.f;          // F16: 2^-11 / (the scale B was split with)
   int64_t M = 0;
   int N = 0;
-  int Kp = 0;                     // % 4 == 0
+  int Kp = 0;                     // % 4 == 0 (TF32), % 8 == 0 (F16)
   GemmEpilogue epi;
 };
 
@@ -52,12 +59,21 @@ struct GemmProblem {
 int encode_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
                 const uint64_t* strides, const uint32_t* box, int swizzle128);
 
-// Encodes a TMA tensor map (CUtensorMap, passed as void*) over a TF32 pair
-// [2][rows][Kp] with box [2][box_rows][BK] and the swizzle of a BK*4-byte row.
+// Same with FP16 elements when f16 != 0.
+int encode_tmap_typed(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides, const uint32_t* box, int swizzle128, int f16);
+
+// Encodes a TMA tensor map over a TF32 pair [2][rows][Kp] with box
+// [2][box_rows][BK] and the swizzle of a BK*4-byte row.
 int make_pair_map(CUtensorMap* map, const float* pair, int64_t rows, int Kp, int box_rows,
                   int BK);
+// Tensor map over [planes][rows][Kp] (fp32, or fp16 when f16 != 0), box = all
+// planes x box_rows x BK, swizzle of one BK-element row.
+int make_planes_map(CUtensorMap* map, const void* base, int64_t rows, int Kp, int planes,
+                    int box_rows, int BK, int f16);
 
-// Launches the TF32x3 tcgen05 GEMM; returns a vitb200 status code.
+// Launches the tcgen05 GEMM (TF32x3 on TF32 pairs, or the three-product FP16
+// split); returns a vitb200 status code.
 int gemm_pairs_launch(const GemmProblem& p, cudaStream_t stream);
 // Raises shared-memory limits of the GEMM kernels on the current device.
 int gemm_prepare_device();
@@ -72,9 +88,15 @@ int device_num_sms();
 // Elementwise / normalisation launchers (elementwise.cu).
 int split_tf32_launch(const float* x, int64_t rows, int cols, int64_t ldx, float* pair, int ldp,
                       cudaStream_t s);
+// x[rows][cols] * scale -> FP16 split planes out[nplanes][rows][ldo] (hi, lo*2^11,
+// and with nplanes == 3 hi*2^11); columns cols..ldo-1 are zero filled. Values
+// whose scaled magnitude reaches the split's limit raise the device error.
+int split_f16_launch(const float* x, int64_t rows, int cols, int64_t ldx, float scale,
+                     uint16_t* out, int64_t ldo, int nplanes, cudaStream_t s);
 int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const float* beta,
                      float* y, int64_t ldy, float* y_pair, int64_t pair_ld, int64_t pair_plane,
-                     int64_t rows, int E, float eps, cudaStream_t s);
+                     int64_t rows, int E, float eps, cudaStream_t s, uint16_t* y_h16 = nullptr,
+                     int64_t h16_ld = 0, int64_t h16_plane = 0);
 int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair, cudaStream_t s);
 int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const float* patches,
                    float* out, int B, int P, int E, cudaStream_t s);
@@ -83,14 +105,16 @@ int gemm_k0_launch(const GemmProblem& p, cudaStream_t s);
 // Raises the attention kernel's shared-memory limit on the current device.
 int attention_prepare_device();
 
-// Attention (attention.cu) on TF32 pairs. q_pair / k_pair are [2][B*T][ld]
+// Attention (attention.cu) on TF32 pairs, writing fp32 O, its TF32 pair and/or
+// its FP16 split. q_pair / k_pair are [2][B*T][ld]
 // buffers (they may be the same buffer), head h of q at columns q_col + h*64.., of
 // k at k_col + h*64..; vt_pair is V transposed per (image, head),
 // [2][B*heads][64][T4] with T4 = T rounded up to 4.
 int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* k_pair,
                      int64_t k_ld, int k_col, const float* vt_pair, float* o, int64_t ldo,
                      float* o_pair, int64_t pair_ld, int64_t pair_plane, int B, int T, int heads,
-                     float scale, cudaStream_t s);
+                     float scale, cudaStream_t s, uint16_t* o_h16 = nullptr, int64_t h16_ld = 0,
+                     int64_t h16_plane = 0);
 // V[B*T][ldv] (head h at columns h*64..) -> vt pair [2][B*heads][64][T4].
 int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int heads, float* vt_pair,
                              cudaStream_t s);

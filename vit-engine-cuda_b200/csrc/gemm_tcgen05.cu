@@ -49,6 +49,8 @@ struct GemmArgs {
   int vec_out;     // fp32 output rows are 16-byte aligned (float4 stores)
   int vec_pair;    // pair rows are 16-byte aligned
   int vec_res;     // residual rows are 16-byte aligned
+  int vec_h16;     // FP16-pair rows are 16-byte aligned
+  float acc_scale; // F16 kernels: multiplies the accumulator (a power of two)
   int* err;
   GemmEpilogue epi;
 };
@@ -67,14 +69,20 @@ constexpr uint32_t kEpiRegs = 224;
 static_assert(128 * kCtrlRegs + 256 * kEpiRegs == 384 * 168, "register split");
 constexpr int kTmemAll = 512;  // TMEM columns: chunk accumulators of BN columns each
 
-template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 struct GemmCfg {
   // PAIR: the two CTAs of a cluster share a 256 x BN tile; each holds 128 rows
   // of A, BN/2 rows of B and 128 x BN accumulators in its own TMEM.
+  // F16: operands are FP16 splits (A: hi, lo; B: hi, lo, hi*2^11), TF32
+  // otherwise (A and B: hi, lo).
+  static constexpr int kEs = F16 ? 2 : 4;       // bytes per element
+  static constexpr int kRowBytes = BK * kEs;    // one K-major tile row
+  static constexpr int kMmaK = F16 ? 16 : 8;    // K per tcgen05.mma (32 bytes)
+  static constexpr int kBPlanes = F16 ? 3 : 2;
   static constexpr int kBRows = PAIR ? BN / 2 : BN;
-  static constexpr int kAPlane = kBM * BK * 4;  // bytes of one A plane (hi or lo)
-  static constexpr int kBPlane = kBRows * BK * 4;
-  static constexpr int kStageBytes = 2 * kAPlane + 2 * kBPlane;
+  static constexpr int kAPlane = kBM * BK * kEs;  // bytes of one A plane
+  static constexpr int kBPlane = kBRows * BK * kEs;
+  static constexpr int kStageBytes = 2 * kAPlane + kBPlanes * kBPlane;
   // Per epilogue warp: a 32 x 32 transpose buffer (row pitch 36 floats keeps the
   // 16-byte row writes and the transposed reads free of bank conflicts).
   static constexpr int kStagingBytes = kEpiWarps * 32 * kStgPitch * 4;
@@ -83,10 +91,10 @@ struct GemmCfg {
   static constexpr int kTmemCols = kTmemAll;
   static constexpr int kHalfN = BN / 2;           // columns per epilogue warpgroup
   static constexpr int kTileM = PAIR ? 2 * kBM : kBM;
-  static constexpr uint32_t kIdesc = make_idesc_tf32(kTileM, BN);
+  static constexpr uint32_t kIdesc = F16 ? make_idesc_f16(kTileM, BN) : make_idesc_tf32(kTileM, BN);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(!PAIR || BN % 16 == 0, "pair N");
-  static_assert(BK * 4 == 128 || BK * 4 == 64, "BK row must be a 64B or 128B swizzle span");
+  static_assert(kRowBytes == 128 || kRowBytes == 64, "BK row must be a 64B or 128B swizzle span");
   static_assert((kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols >= 32 && kTmemCols <= 512,
                 "TMEM columns must be a power of two in [32, 512]");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -101,6 +109,7 @@ struct GemmCfg {
 // Row-contiguous outputs go through the warp's transpose buffer `stg`, so every
 // global access instruction covers four whole 128-byte row segments instead of
 // sixteen bytes of 32 different rows.
+template <bool F16>
 __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base, int lane, int n0,
                                               float (&v)[32], float* stg) {
   const GemmEpilogue& e = a.epi;
@@ -108,6 +117,12 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
   const int64_t m = m_base + lane;
   const bool row_ok = m < a.M;
   const bool full = (n0 + 32 <= N);
+
+  if constexpr (F16) {
+    // Undo the operand scales: exact, a power of two.
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = v[j] * a.acc_scale;
+  }
 
   if (e.bias != nullptr) {
 #pragma unroll
@@ -149,7 +164,8 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
   }
 
   const bool staged = full && e.mode != kModePatch && (!e.out || a.vec_out) &&
-                      (!e.out_pair || a.vec_pair) && (!e.residual || a.vec_res);
+                      (!e.out_pair || a.vec_pair) && (!e.residual || a.vec_res) &&
+                      (!e.out_h16 || a.vec_h16);
   if (staged) {
     const int rsub = lane >> 3;        // row within a group of four
     const int c4 = (lane & 7) * 4;     // this lane's float4 within a 32-column row
@@ -211,6 +227,38 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
       }
       flush(e.out_pair + e.pair_plane, e.ldp);
     }
+    if (e.out_h16 != nullptr) {
+      // Row buffer: words 0-15 = hi halves of the 32 columns, 16-31 = lo
+      // halves. Lanes 0-3 of each group of eight store a row's hi (64 B),
+      // lanes 4-7 its lo, four rows per instruction.
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          __half h0, l0, h1, l1;
+          h16_split(v[j + 2 * t], h0, l0);
+          h16_split(v[j + 2 * t + 1], h1, l1);
+          hw[t] = pack_h2(h0, h1);
+          lw[t] = pack_h2(l0, l1);
+        }
+        *reinterpret_cast<uint4*>(my_row + j / 2) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(my_row + 16 + j / 2) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+      __syncwarp();
+      const int plane = c4 >> 4;     // 0: hi, 1: lo
+      const int hcol = (c4 & 15) * 2;  // first of this lane's eight columns
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = 4 * k + rsub;
+        const int64_t mr = m_base + r;
+        const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgPitch + c4);
+        if (mr < a.M)
+          *reinterpret_cast<uint4*>(e.out_h16 + plane * e.h16_plane + mr * e.ldh + col_base +
+                                    hcol) = t;
+      }
+      __syncwarp();
+    }
     return;
   }
 
@@ -258,6 +306,13 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
         pl[j] = l;
       }
   }
+  if (e.out_h16 != nullptr) {
+    __half* ph = reinterpret_cast<__half*>(e.out_h16) + out_row * e.ldh + col_base;
+    __half* pl = ph + e.h16_plane;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) h16_split(v[j], ph[j], pl[j]);
+  }
 }
 
 // TMEM chunk buffer of chunk j of this CTA's local tile `local`: chunks use
@@ -295,11 +350,11 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
   }
 }
 
-template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
-  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB, PAIR>;
+  using Cfg = GemmCfg<F16, BN, BK, STAGES, CHUNK_KB, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -450,23 +505,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_lo = a_hi + Cfg::kAPlane;
           const uint32_t b_hi = a_hi + 2 * Cfg::kAPlane;
           const uint32_t b_lo = b_hi + Cfg::kBPlane;
-#pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint32_t koff = static_cast<uint32_t>(kk * 32);  // 8 TF32 = 32 bytes
-            const uint64_t dah = make_sdesc_kmajor(a_hi + koff, BK * 4);
-            const uint64_t dal = make_sdesc_kmajor(a_lo + koff, BK * 4);
-            const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, BK * 4);
-            const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, BK * 4);
-            const uint32_t acc0 = (chunk_first && kk == 0) ? 0u : 1u;
-            if constexpr (PAIR) {
-              umma_tf32_pair(d_tmem, dal, dbh, Cfg::kIdesc, acc0);  // lo * hi
-              umma_tf32_pair(d_tmem, dah, dbl, Cfg::kIdesc, 1u);    // hi * lo
-              umma_tf32_pair(d_tmem, dah, dbh, Cfg::kIdesc, 1u);    // hi * hi
+          // hi * hi: TF32 uses B's hi plane; F16 its third plane, hi * 2^11.
+          const uint32_t b_hh = F16 ? b_hi + 2 * Cfg::kBPlane : b_hi;
+          auto mma = [&](uint64_t da, uint64_t db, uint32_t acc) {
+            if constexpr (F16 && PAIR) {
+              umma_f16_pair(d_tmem, da, db, Cfg::kIdesc, acc);
+            } else if constexpr (F16) {
+              umma_f16(d_tmem, da, db, Cfg::kIdesc, acc);
+            } else if constexpr (PAIR) {
+              umma_tf32_pair(d_tmem, da, db, Cfg::kIdesc, acc);
             } else {
-              umma_tf32(d_tmem, dal, dbh, Cfg::kIdesc, acc0);
-              umma_tf32(d_tmem, dah, dbl, Cfg::kIdesc, 1u);
-              umma_tf32(d_tmem, dah, dbh, Cfg::kIdesc, 1u);
+              umma_tf32(d_tmem, da, db, Cfg::kIdesc, acc);
             }
+          };
+#pragma unroll
+          for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+            const uint32_t koff = static_cast<uint32_t>(kk * 32);  // one MMA's K = 32 bytes
+            const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
+            const uint64_t dal = make_sdesc_kmajor(a_lo + koff, Cfg::kRowBytes);
+            const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
+            const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, Cfg::kRowBytes);
+            const uint64_t dbhh = make_sdesc_kmajor(b_hh + koff, Cfg::kRowBytes);
+            const uint32_t acc0 = (chunk_first && kk == 0) ? 0u : 1u;
+            mma(dal, dbh, acc0);  // lo * hi
+            mma(dah, dbl, 1u);    // hi * lo
+            mma(dah, dbhh, 1u);   // hi * hi
           }
           commit(&empty_bar[stage]);  // frees the stage once these MMAs finish
           if (++stage == STAGES) {
@@ -543,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int n0 = n_blk * BN + col0 + q * 32;
           if (n0 < args.N) {
             float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[0]);
-            epilogue_slab(args, m_base, lane, n0, part, stg);
+            epilogue_slab<F16>(args, m_base, lane, n0, part, stg);
           }
 #pragma unroll
           for (int c = 0; c + 32 < Cfg::kHalfN; ++c) sum[c] = sum[c + 32];
@@ -591,6 +654,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 int encode_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
                 const uint64_t* strides, const uint32_t* box, int swizzle128) {
+  return encode_tmap_typed(map, rank, base, dims, strides, box, swizzle128, 0);
+}
+
+int encode_tmap_typed(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides, const uint32_t* box, int swizzle128, int f16) {
   auto enc = encode_fn();
   if (enc == nullptr) return VITB200_E_NO_TMA;
   if (rank < 1 || rank > 5) return VITB200_E_INVALID_ARG;
@@ -604,7 +672,8 @@ int encode_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* di
     if (i + 1 < rank) st[i] = static_cast<cuuint64_t>(strides[i]);
   }
   const CUtensorMapSwizzle sw = swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank),
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = enc(map, dt, static_cast<cuuint32_t>(rank),
                    const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : VITB200_E_NO_TMA;
@@ -614,39 +683,54 @@ int encode_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* di
 // swizzle matching a BK*4-byte row.
 int make_pair_map(CUtensorMap* map, const float* pair, int64_t rows, int Kp, int box_rows,
                   int BK) {
-  const uint64_t dims[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(rows), 2};
-  const uint64_t strides[2] = {static_cast<uint64_t>(Kp) * 4,
-                               static_cast<uint64_t>(rows) * static_cast<uint64_t>(Kp) * 4};
-  const uint32_t box[3] = {static_cast<uint32_t>(BK), static_cast<uint32_t>(box_rows), 2};
-  return encode_tmap(map, 3, pair, dims, strides, box, BK * 4 == 128);
+  return make_planes_map(map, pair, rows, Kp, 2, box_rows, BK, 0);
+}
+
+// Tensor map over `planes` planes [planes][rows][Kp] of fp32 (f16 = 0) or fp16
+// elements, box = all planes x box_rows x BK, swizzle of one BK-element row.
+int make_planes_map(CUtensorMap* map, const void* base, int64_t rows, int Kp, int planes,
+                    int box_rows, int BK, int f16) {
+  const uint64_t es = f16 ? 2 : 4;
+  const uint64_t dims[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(rows),
+                            static_cast<uint64_t>(planes)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(Kp) * es,
+                               static_cast<uint64_t>(rows) * static_cast<uint64_t>(Kp) * es};
+  const uint32_t box[3] = {static_cast<uint32_t>(BK), static_cast<uint32_t>(box_rows),
+                           static_cast<uint32_t>(planes)};
+  return encode_tmap_typed(map, 3, base, dims, strides, box, BK * es == 128, f16);
 }
 
 namespace {
 
 struct Variant {
-  int bn, bk, stages, chunk_kb, pair;
+  int f16, bn, bk, stages, chunk_kb, pair;
 };
-// Index 1.. are selectable with gemm_set_variant; 0 = automatic.
+// Index 1.. are selectable with gemm_set_variant; 0 = automatic. 1-8 take TF32
+// pairs, 9-12 FP16 splits; a forced variant of the other operand kind is ignored.
 constexpr Variant kVariants[] = {
-    {0, 0, 0, 0, 0},    {128, 32, 2, 4, 0}, {128, 16, 5, 8, 0}, {64, 32, 3, 4, 0},
-    {128, 32, 2, 2, 0}, {256, 16, 3, 8, 0}, {256, 32, 2, 4, 1}, {256, 16, 5, 8, 1},
-    {256, 16, 5, 16, 1},
+    {0, 0, 0, 0, 0, 0},     {0, 128, 32, 2, 4, 0}, {0, 128, 16, 5, 8, 0}, {0, 64, 32, 3, 4, 0},
+    {0, 128, 32, 2, 2, 0},  {0, 256, 16, 3, 8, 0}, {0, 256, 32, 2, 4, 1}, {0, 256, 16, 5, 8, 1},
+    {0, 256, 16, 5, 16, 1}, {1, 256, 64, 2, 2, 1}, {1, 128, 64, 2, 2, 0}, {1, 64, 64, 3, 2, 0},
+    {1, 256, 32, 4, 4, 1},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 constexpr int kPairVariant = 6;
+constexpr int kF16PairVariant = 9;
 int g_forced_variant = 0;
 
 // Cluster-of-two slots that fit on the device at once, per device (0 = not
 // queried yet).
 int g_pair_slots[64] = {};
 
-template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
-  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB, PAIR>;
+  using Cfg = GemmCfg<F16, BN, BK, STAGES, CHUNK_KB, PAIR>;
   CUtensorMap ta, tb;
-  int st = make_pair_map(&ta, p.a_pair, p.M, p.Kp, kBM, BK);
+  int st = F16 ? make_planes_map(&ta, p.a_h16, p.M, p.Kp, 2, kBM, BK, 1)
+               : make_pair_map(&ta, p.a_pair, p.M, p.Kp, kBM, BK);
   if (st) return st;
-  st = make_pair_map(&tb, p.b_pair, p.N, p.Kp, Cfg::kBRows, BK);
+  st = F16 ? make_planes_map(&tb, p.b_h16, p.N, p.Kp, 3, Cfg::kBRows, BK, 1)
+           : make_pair_map(&tb, p.b_pair, p.N, p.Kp, Cfg::kBRows, BK);
   if (st) return st;
   GemmArgs a;
   a.M = p.M;
@@ -666,6 +750,9 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
                (e.ldp % 4 == 0) && (e.pair_plane % 4 == 0);
   a.vec_res = (e.residual != nullptr) && (reinterpret_cast<uintptr_t>(e.residual) % 16 == 0) &&
               (e.ldr % 4 == 0);
+  a.vec_h16 = (e.out_h16 != nullptr) && (reinterpret_cast<uintptr_t>(e.out_h16) % 16 == 0) &&
+              (e.ldh % 8 == 0) && (e.h16_plane % 8 == 0);
+  a.acc_scale = F16 ? p.acc_scale : 1.f;
   a.err = err;
   a.epi = e;
   if constexpr (PAIR) {
@@ -685,7 +772,7 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
     int slots = (dev >= 0 && dev < 64) ? g_pair_slots[dev] : 0;
     if (slots <= 0) {
       cfg.gridDim = dim3(2 * static_cast<unsigned>(device_num_sms() / 2));
-      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>,
+      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>,
                                          &cfg) != cudaSuccess ||
           slots <= 0) {
         (void)cudaGetLastError();
@@ -694,40 +781,39 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
       if (dev >= 0 && dev < 64) g_pair_slots[dev] = slots;
     }
     cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
-    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>,
+    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>,
                                         ta, tb, a));
     count_launch();
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_num_sms()));
-    gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>
+    gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>
         <<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, a);
     count_launch();
     return cuda_status(cudaGetLastError());
   }
 }
 
-template <int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 int set_smem_attr() {
-  using Cfg = GemmCfg<BN, BK, STAGES, CHUNK_KB, PAIR>;
-  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, STAGES, CHUNK_KB, PAIR>,
+  using Cfg = GemmCfg<F16, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           Cfg::kSmemBytes));
 }
 
-int pick_variant(int64_t M, int N, const GemmEpilogue& e) {
+int pick_variant(int64_t M, int N, bool f16) {
   // Large problems: 256 x 128 tiles on CTA pairs (each SM streams half of B,
   // so operand traffic per FLOP matches a 256-wide tile). Small ones (batch-1
   // latency): the single-CTA tile width that minimises (waves of tiles) x
   // (tile width); a partial last wave costs a full one.
   const int sms = device_num_sms();
-  (void)e;
-  if (M >= 1024) return kPairVariant;
+  if (M >= 1024) return f16 ? kF16PairVariant : kPairVariant;
   const int64_t m_tiles = (M + kBM - 1) / kBM;
-  int best = 1;
+  int best = f16 ? 10 : 1;
   int64_t best_cost = -1;
-  const int cands[2] = {1, 3};  // BN = 128, 64
+  const int cands[2] = {f16 ? 10 : 1, f16 ? 11 : 3};  // BN = 128, 64
   for (int c : cands) {
     const int bn = kVariants[c].bn;
     const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
@@ -750,21 +836,27 @@ int gemm_set_variant(int v) {
 }
 
 int gemm_prepare_device() {
-  int st = set_smem_attr<128, 32, 2, 4, false>();
-  if (!st) st = set_smem_attr<128, 16, 5, 8, false>();
-  if (!st) st = set_smem_attr<64, 32, 3, 4, false>();
-  if (!st) st = set_smem_attr<128, 32, 2, 2, false>();
-  if (!st) st = set_smem_attr<256, 16, 3, 8, false>();
-  if (!st) st = set_smem_attr<256, 32, 2, 4, true>();
-  if (!st) st = set_smem_attr<256, 16, 5, 8, true>();
-  if (!st) st = set_smem_attr<256, 16, 5, 16, true>();
+  int st = set_smem_attr<false, 128, 32, 2, 4, false>();
+  if (!st) st = set_smem_attr<false, 128, 16, 5, 8, false>();
+  if (!st) st = set_smem_attr<false, 64, 32, 3, 4, false>();
+  if (!st) st = set_smem_attr<false, 128, 32, 2, 2, false>();
+  if (!st) st = set_smem_attr<false, 256, 16, 3, 8, false>();
+  if (!st) st = set_smem_attr<false, 256, 32, 2, 4, true>();
+  if (!st) st = set_smem_attr<false, 256, 16, 5, 8, true>();
+  if (!st) st = set_smem_attr<false, 256, 16, 5, 16, true>();
+  if (!st) st = set_smem_attr<true, 256, 64, 2, 2, true>();
+  if (!st) st = set_smem_attr<true, 128, 64, 2, 2, false>();
+  if (!st) st = set_smem_attr<true, 64, 64, 3, 2, false>();
+  if (!st) st = set_smem_attr<true, 256, 32, 4, 4, true>();
   if (!st && encode_fn() == nullptr) st = VITB200_E_NO_TMA;
   return st;
 }
 
 int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
-  if (p.M < 0 || p.N < 0 || p.Kp < 0 || (p.Kp % 4) != 0) return VITB200_E_INVALID_ARG;
-  if (p.epi.out == nullptr && p.epi.out_pair == nullptr) return VITB200_E_INVALID_ARG;
+  const bool f16 = p.f16 != 0;
+  if (p.M < 0 || p.N < 0 || p.Kp < 0 || (p.Kp % (f16 ? 8 : 4)) != 0) return VITB200_E_INVALID_ARG;
+  if (p.epi.out == nullptr && p.epi.out_pair == nullptr && p.epi.out_h16 == nullptr)
+    return VITB200_E_INVALID_ARG;
   if (p.M == 0 || p.N == 0) return 0;
   if (p.epi.mode == kModeSplit3 && (p.epi.e_split <= 0 || p.epi.e_split % 32 != 0))
     return VITB200_E_UNSUPPORTED;
@@ -776,21 +868,28 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
   if (p.epi.mode == kModePatch && (p.epi.P <= 0 || p.epi.T != p.epi.P + 1 || !p.epi.pos))
     return VITB200_E_INVALID_ARG;
   if (p.Kp == 0) return gemm_k0_launch(p, s);
-  if (p.a_pair == nullptr || p.b_pair == nullptr) return VITB200_E_INVALID_ARG;
-  if (reinterpret_cast<uintptr_t>(p.a_pair) % 16 || reinterpret_cast<uintptr_t>(p.b_pair) % 16)
+  const void* a_ptr = f16 ? static_cast<const void*>(p.a_h16) : p.a_pair;
+  const void* b_ptr = f16 ? static_cast<const void*>(p.b_h16) : p.b_pair;
+  if (a_ptr == nullptr || b_ptr == nullptr) return VITB200_E_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(a_ptr) % 16 || reinterpret_cast<uintptr_t>(b_ptr) % 16)
     return VITB200_E_ALIGNMENT;
   int* err = device_error_word();
   if (err == nullptr) return VITB200_E_INVALID_ARG;
-  const int v = g_forced_variant ? g_forced_variant : pick_variant(p.M, p.N, p.epi);
+  int v = g_forced_variant;
+  if (v == 0 || (kVariants[v].f16 != 0) != f16) v = pick_variant(p.M, p.N, f16);
   switch (v) {
-    case 1: return launch_variant<128, 32, 2, 4, false>(p, err, s);
-    case 2: return launch_variant<128, 16, 5, 8, false>(p, err, s);
-    case 3: return launch_variant<64, 32, 3, 4, false>(p, err, s);
-    case 4: return launch_variant<128, 32, 2, 2, false>(p, err, s);
-    case 5: return launch_variant<256, 16, 3, 8, false>(p, err, s);
-    case 6: return launch_variant<256, 32, 2, 4, true>(p, err, s);
-    case 7: return launch_variant<256, 16, 5, 8, true>(p, err, s);
-    case 8: return launch_variant<256, 16, 5, 16, true>(p, err, s);
+    case 1: return launch_variant<false, 128, 32, 2, 4, false>(p, err, s);
+    case 2: return launch_variant<false, 128, 16, 5, 8, false>(p, err, s);
+    case 3: return launch_variant<false, 64, 32, 3, 4, false>(p, err, s);
+    case 4: return launch_variant<false, 128, 32, 2, 2, false>(p, err, s);
+    case 5: return launch_variant<false, 256, 16, 3, 8, false>(p, err, s);
+    case 6: return launch_variant<false, 256, 32, 2, 4, true>(p, err, s);
+    case 7: return launch_variant<false, 256, 16, 5, 8, true>(p, err, s);
+    case 8: return launch_variant<false, 256, 16, 5, 16, true>(p, err, s);
+    case 9: return launch_variant<true, 256, 64, 2, 2, true>(p, err, s);
+    case 10: return launch_variant<true, 128, 64, 2, 2, false>(p, err, s);
+    case 11: return launch_variant<true, 64, 64, 3, 2, false>(p, err, s);
+    case 12: return launch_variant<true, 256, 32, 4, 4, true>(p, err, s);
     default: return VITB200_E_UNSUPPORTED;
   }
 }

@@ -38,7 +38,11 @@ class VitB200Error(RuntimeError):
 class BlockParams(ctypes.Structure):
     _fields_ = [(name, c_void_p) for name in (
         "norm1_w", "norm1_b", "qkv_w_pair", "qkv_b", "proj_w_pair", "proj_b",
-        "norm2_w", "norm2_b", "fc1_w_pair", "fc1_b", "fc2_w_pair", "fc2_b")]
+        "norm2_w", "norm2_b", "fc1_w_pair", "fc1_b", "fc2_w_pair", "fc2_b")] + [
+        ("qkv_w_f16", c_void_p), ("qkv_acc_scale", c_float),
+        ("proj_w_f16", c_void_p), ("proj_acc_scale", c_float),
+        ("fc1_w_f16", c_void_p), ("fc1_acc_scale", c_float),
+        ("fc2_w_f16", c_void_p), ("fc2_acc_scale", c_float)]
 
 
 class VitParams(ctypes.Structure):
@@ -63,6 +67,9 @@ _SIGNATURES = {
     "vitb200_launch_count": (ctypes.c_uint64, []),
     "vitb200_set_gemm_variant": (c_int, [c_int]),
     "vitb200_split_tf32": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int, _P]),
+    "vitb200_split_f16": (c_int, [_P, c_int64, c_int, c_int64, c_float, _P, c_int64, c_int, _P]),
+    "vitb200_gemm_f16": (c_int, [_P, _P, c_float, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int,
+                                 c_int, _P]),
     "vitb200_layernorm": (c_int, [_P, _P, _P, _P, c_int64, c_int, c_float, _P]),
     "vitb200_gemm_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "vitb200_gemm": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int, c_int, c_int, _P, c_size_t, _P]),

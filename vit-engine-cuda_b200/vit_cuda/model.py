@@ -9,8 +9,11 @@ Behind that surface the forward is one call into libvitb200.so
 current stream: im2col -> patch GEMM (+bias +pos) -> 12 x [LN1 -> QKV GEMM ->
 attention -> proj GEMM (+bias +residual) -> LN2 -> fc1 GEMM (+bias +GELU) ->
 fc2 GEMM (+bias +residual)] -> LN(CLS rows) -> head GEMM. The linear weights are
-split once per device into TF32 hi/lo pairs (``prepare``); activations are
-split by the kernel that produces them.
+split once per device (``prepare``); activations are split by the kernel that
+produces them. The four block GEMMs run on FP16 splits (three FP16 tensor-core
+products, FP32 accuracy at twice the TF32 rate) wherever the weights bound
+their input below the split's range, and on TF32 pairs (TF32x3) otherwise;
+``operands="tf32"`` keeps every GEMM on TF32 pairs.
 
 ``ViTBlockCUDA.forward`` keeps the reference's op-by-op block (the ``_C`` ops)
 for callers that drive blocks themselves.
@@ -26,6 +29,7 @@ import torch.nn as nn
 
 from . import _C, _lib
 from ._lib import BlockParams, VitParams, lib
+from .split import F16_SAFE_BOUND, block_input_bounds, f16_weight, f16_weight_ok
 
 _BLOCK_KEYS = [
     ("norm1_gamma", "norm1.weight"), ("norm1_beta", "norm1.bias"),
@@ -74,8 +78,11 @@ def _split_pair(w: torch.Tensor) -> torch.Tensor:
 
 
 class ViTCUDA(nn.Module):
-    def __init__(self, num_classes=1000, state_dict=None, pretrained=True):
+    def __init__(self, num_classes=1000, state_dict=None, pretrained=True, operands="auto"):
         super().__init__()
+        if operands not in ("auto", "tf32"):
+            raise ValueError("operands must be 'auto' or 'tf32'")
+        self.operands = operands
         if state_dict is None:
             try:
                 import timm  # noqa: F401  (reference model.py:67-69)
@@ -121,9 +128,11 @@ class ViTCUDA(nn.Module):
         return (self.patch_weight.device, ptrs)
 
     def prepare(self, force: bool = False):
-        """Splits the linear weights into TF32 pairs on their device and builds
-        the C parameter block. Runs once per device / weight storage; call it
-        again with force=True after modifying weights in place."""
+        """Splits the linear weights on their device (FP16 splits where the
+        block's input bounds allow, TF32 pairs otherwise; ``gemm_operands``
+        records the choice per block) and builds the C parameter block. Runs
+        once per device / weight storage; call it again with force=True after
+        modifying weights in place."""
         key = self._source_key()
         if not force and self._prepared is not None and self._prepared[0] == key:
             return self._prepared
@@ -137,18 +146,34 @@ class ViTCUDA(nn.Module):
             pairs = {"patch": _split_pair(self.patch_weight), "head": _split_pair(self.head_weight)}
             blocks = (BlockParams * len(self.blocks))()
             keep = []
+            self.gemm_operands = []
             for i, blk in enumerate(self.blocks):
-                qkv, proj = _split_pair(blk.qkv_weight), _split_pair(blk.proj_weight)
-                fc1, fc2 = _split_pair(blk.fc1_weight), _split_pair(blk.fc2_weight)
-                keep += [qkv, proj, fc1, fc2]
+                bounds = block_input_bounds(blk, 768)
+                w = {}
+                kinds = {}
+                for name in ("qkv", "proj", "fc1", "fc2"):
+                    weight = getattr(blk, f"{name}_weight")
+                    if (self.operands == "auto" and bounds[name] < F16_SAFE_BOUND
+                            and f16_weight_ok(weight)):
+                        planes, acc_scale = f16_weight(weight.contiguous())
+                        w[name] = (None, planes, acc_scale)
+                        kinds[name] = "f16"
+                    else:
+                        w[name] = (_split_pair(weight), None, 0.0)
+                        kinds[name] = "tf32"
+                    keep += [t for t in w[name][:2] if t is not None]
+                self.gemm_operands.append(kinds)
                 vecs = [blk.norm1_gamma, blk.norm1_beta, blk.qkv_bias, blk.proj_bias,
                         blk.norm2_gamma, blk.norm2_beta, blk.fc1_bias, blk.fc2_bias]
                 vecs = [v.contiguous() for v in vecs]
                 keep += vecs
+                ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
                 blocks[i] = BlockParams(
-                    vecs[0].data_ptr(), vecs[1].data_ptr(), qkv.data_ptr(), vecs[2].data_ptr(),
-                    proj.data_ptr(), vecs[3].data_ptr(), vecs[4].data_ptr(), vecs[5].data_ptr(),
-                    fc1.data_ptr(), vecs[6].data_ptr(), fc2.data_ptr(), vecs[7].data_ptr())
+                    vecs[0].data_ptr(), vecs[1].data_ptr(), ptr(w["qkv"][0]), vecs[2].data_ptr(),
+                    ptr(w["proj"][0]), vecs[3].data_ptr(), vecs[4].data_ptr(), vecs[5].data_ptr(),
+                    ptr(w["fc1"][0]), vecs[6].data_ptr(), ptr(w["fc2"][0]), vecs[7].data_ptr(),
+                    ptr(w["qkv"][1]), w["qkv"][2], ptr(w["proj"][1]), w["proj"][2],
+                    ptr(w["fc1"][1]), w["fc1"][2], ptr(w["fc2"][1]), w["fc2"][2])
             vecs = {n: getattr(self, n).contiguous() for n in
                     ("patch_bias", "cls_token", "pos_embed", "norm_gamma", "norm_beta",
                      "head_bias")}
