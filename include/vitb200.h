@@ -148,8 +148,9 @@ int vitb200_gemm_pairs(const float* a_pair, const float* w_pair, const float* bi
  * nplanes (2 or 3) planes of planes[nplanes][rows][ldp] fp16 (ldp % 8 == 0,
  * zero past cols): hi = fp16(x*scale), lo = fp16((x*scale - hi) * 2^11) and,
  * with nplanes == 3, hi * 2^11 (the third plane a GEMM's W operand needs).
- * Scaled magnitudes must stay below 32768; a larger or non-finite value sets
- * the device error (vitb200_device_error) instead of failing silently.
+ * Scaled magnitudes must stay below 32768 (below 16 with nplanes == 3); a
+ * larger or non-finite value sets the device error (vitb200_device_error)
+ * instead of failing silently.
  * No reference counterpart: operand preparation of vitb200_gemm_f16. */
 int vitb200_split_f16(const float* x, int64_t rows, int cols, int64_t ldx, float scale,
                       uint16_t* planes, int64_t ldp, int nplanes, void* stream);
@@ -194,6 +195,20 @@ int vitb200_attention(const float* q, const float* k, const float* v, float* o,
                       int B, int T, int heads, int64_t ldq, int64_t ldk,
                       int64_t ldv, int64_t ldo, float scale, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/* The same attention with FP16-split operands (three FP16 tensor-core
+ * products per multiply, FP32 accuracy; the form the model's block path
+ * uses). k and v are multiplied by k_scale and v_scale (powers of two, undone
+ * exactly) before the split; the caller chooses them so that |k * k_scale| and
+ * |v * v_scale| stay below 16 and |q| below 32768 (larger values set the
+ * device error). The workspace holds the FP16 splits of q, k and V^T. No
+ * reference counterpart beyond flash_attn_2_forward_cuda's semantics. */
+size_t vitb200_attention_f16_workspace_bytes(int B, int T, int heads);
+int vitb200_attention_f16(const float* q, const float* k, const float* v, float* o,
+                          int B, int T, int heads, int64_t ldq, int64_t ldk,
+                          int64_t ldv, int64_t ldo, float scale, float k_scale,
+                          float v_scale, void* workspace, size_t workspace_bytes,
+                          void* stream);
 
 /* Patch embedding as im2col + TF32x3 GEMM: img[B][C][H][W] (16x16 patches,
  * vector order (c, py, px)), weights [E][C*256] -> out[B][P][E] (+ bias when
@@ -245,6 +260,13 @@ typedef struct vitb200_block_params {
     const uint16_t* proj_w_f16; float proj_acc_scale;
     const uint16_t* fc1_w_f16;  float fc1_acc_scale;
     const uint16_t* fc2_w_f16;  float fc2_acc_scale;
+    /* attn_f16 != 0: the attention runs on FP16 splits (as
+     * vitb200_attention_f16), its q, k, v written by the QKV GEMM multiplied by
+     * q_scale, k_scale, v_scale (powers of two). The caller guarantees
+     * |q * q_scale| < 32768 and |k * k_scale|, |v * v_scale| < 16 (bounds as
+     * above). 0: TF32 pairs. */
+    int attn_f16;
+    float q_scale, k_scale, v_scale;
 } vitb200_block_params;
 
 typedef struct vitb200_vit_params {

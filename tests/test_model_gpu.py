@@ -137,7 +137,8 @@ def test_384_tokens577(cuda):
 
 def test_operand_choice(case224, cuda):
     """Random-init ViT-B/16 weights bound every block GEMM input far below the
-    FP16 split's range, so all 48 run on FP16 splits by default."""
+    FP16 split's range, so all 48 GEMMs and the 12 attentions run on FP16
+    splits by default."""
     _, _, _, _, model = case224
     model.prepare()
     assert len(model.gemm_operands) == 12
@@ -166,7 +167,8 @@ def test_out_of_range_block_falls_back_to_tf32(cuda):
     ref = orc.vit_forward(img, state)
     model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
     model.prepare()
-    assert model.gemm_operands[11] == {"qkv": "f16", "proj": "f16", "fc1": "tf32", "fc2": "tf32"}
+    assert model.gemm_operands[11] == {"qkv": "f16", "proj": "f16", "fc1": "tf32", "fc2": "tf32",
+                                       "attn": "f16"}
     assert all(k == "f16" for blk in model.gemm_operands[:11] for k in blk.values())
     with torch.no_grad():
         out = model(img.to(cuda)).double().cpu()

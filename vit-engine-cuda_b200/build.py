@@ -66,10 +66,11 @@ def compile_one(src: str) -> tuple[str, str]:
 
 
 # Kernels that move registers between warpgroups with setmaxnreg, and the
-# per-thread register count their split assumes (csrc/gemm_tcgen05.cu: 384
-# threads launched at 168 registers; the warpgroups then take 56 and 224). A
-# kernel compiled to any other count would make setmaxnreg.inc wait forever.
-SETMAXNREG_KERNELS = {"gemm_tf32x3_kernel": 168}
+# per-thread register count their split assumes (csrc/gemm_tcgen05.cu,
+# csrc/attention_f16.cu: 384 threads launched at 168 registers; the warpgroups
+# then take 56 and 224). A kernel compiled to any other count would make
+# setmaxnreg.inc wait forever.
+SETMAXNREG_KERNELS = {"gemm_tf32x3_kernel": 168, "attention_f16_kernel": 168}
 
 
 def check_register_split(ptxas_log: str) -> None:

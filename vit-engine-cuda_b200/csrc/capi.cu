@@ -49,6 +49,7 @@ DeviceState* device_state(int* status) {
       d.ready = true;  // gemm_prepare_device() below reads the SM count
       st = gemm_prepare_device();
       if (!st) st = attention_prepare_device();
+      if (!st) st = attention_f16_prepare_device();
       if (st) d.ready = false;
     }
     d.status = st;
@@ -468,6 +469,50 @@ int vitb200_attention(const float* q, const float* k, const float* v, float* o, 
   VITB200_GUARD_END
 }
 
+static size_t vt16_halves(int B, int T, int heads) {
+  const size_t T8 = (static_cast<size_t>(T) + 7) / 8 * 8;
+  return 3 * static_cast<size_t>(B) * heads * 64 * T8;
+}
+
+size_t vitb200_attention_f16_workspace_bytes(int B, int T, int heads) {
+  if (B < 0 || T < 0 || heads <= 0) return 0;
+  Carve c{nullptr, 0};
+  const size_t n = static_cast<size_t>(B) * T * heads * 64;
+  c.take((2 * n + 1) / 2);         // q16: 2 planes of halves
+  c.take((3 * n + 1) / 2);         // k16: 3 planes
+  c.take((vt16_halves(B, T, heads) + 1) / 2);
+  return align_up(c.off, 256);
+}
+
+int vitb200_attention_f16(const float* q, const float* k, const float* v, float* o, int B, int T,
+                          int heads, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo,
+                          float scale, float k_scale, float v_scale, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (B < 0 || T < 0 || heads <= 0 || !q || !k || !v || !o) return VITB200_E_INVALID_ARG;
+  if (!(k_scale > 0.f) || !(v_scale > 0.f)) return VITB200_E_INVALID_ARG;
+  const int64_t width = static_cast<int64_t>(heads) * 64;
+  if (ldq < width || ldk < width || ldv < width || ldo < width) return VITB200_E_INVALID_ARG;
+  if (B == 0 || T == 0) return 0;
+  const int64_t M = static_cast<int64_t>(B) * T;
+  const size_t n = static_cast<size_t>(M) * width;
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  uint16_t* q16 = reinterpret_cast<uint16_t*>(c.take((2 * n + 1) / 2));
+  uint16_t* k16 = reinterpret_cast<uint16_t*>(c.take((3 * n + 1) / 2));
+  uint16_t* vt16 = reinterpret_cast<uint16_t*>(c.take((vt16_halves(B, T, heads) + 1) / 2));
+  if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
+  if (int st = check_ready()) return st;
+  cudaStream_t s = as_stream(stream);
+  if (int st = split_f16_launch(q, M, static_cast<int>(width), ldq, 1.f, q16, width, 2, s))
+    return st;
+  if (int st = split_f16_launch(k, M, static_cast<int>(width), ldk, k_scale, k16, width, 3, s))
+    return st;
+  if (int st = split_transpose_v_f16_launch(v, ldv, B, T, heads, v_scale, vt16, s)) return st;
+  return attention_f16_launch(q16, k16, width, vt16, (T + 7) / 8 * 8, o, ldo, nullptr, 0, 0,
+                              nullptr, 0, 0, B, T, heads, scale, 1.f, k_scale, v_scale, s);
+  VITB200_GUARD_END
+}
+
 // ---------------------------------------------------------------- patch embed
 
 size_t vitb200_patch_embed_workspace_bytes(int B, int C, int H, int W, int E) {
@@ -589,6 +634,8 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
     if ((b.qkv_w_f16 && !(b.qkv_acc_scale > 0.f)) || (b.proj_w_f16 && !(b.proj_acc_scale > 0.f)) ||
         (b.fc1_w_f16 && !(b.fc1_acc_scale > 0.f)) || (b.fc2_w_f16 && !(b.fc2_acc_scale > 0.f)))
       return VITB200_E_INVALID_ARG;
+    if (b.attn_f16 && (!(b.q_scale > 0.f) || !(b.k_scale > 0.f) || !(b.v_scale > 0.f)))
+      return VITB200_E_INVALID_ARG;
   }
   d->P = (p->img_h / 16) * (p->img_w / 16);
   d->T = d->P + 1;
@@ -615,8 +662,10 @@ size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve
   b->x = c->take(static_cast<size_t>(d.M) * D);
   b->pair_a = c->take(2 * std::max(static_cast<size_t>(d.M) * D,
                                    static_cast<size_t>(d.Mp) * d.Kpatch));
+  // qk / vt also hold the FP16 attention's q16 + k16 (5 planes of halves) and vt16.
   b->qk = c->take(2 * static_cast<size_t>(d.M) * 2 * D);
-  b->vt = c->take(vt_pair_floats(batch, d.T, p->num_heads));
+  b->vt = c->take(std::max(vt_pair_floats(batch, d.T, p->num_heads),
+                           (vt16_halves(batch, d.T, p->num_heads) + 1) / 2));
   b->hpair = c->take(2 * static_cast<size_t>(d.M) * p->mlp_dim);
   b->cls_pair = c->take(2 * static_cast<size_t>(batch) * D);
   return align_up(c->off, 256);
@@ -677,6 +726,10 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
   if (int st = layernorm_launch(x, D, w.norm1_w, w.norm1_b, nullptr, 0, f_qkv ? nullptr : b.pair_a,
                                 D, plane, M, D, p->ln_eps, s, f_qkv ? a16 : nullptr, D, plane))
     return st;
+  const int T8 = (d.T + 7) / 8 * 8;
+  uint16_t* q16 = reinterpret_cast<uint16_t*>(b.qk);
+  uint16_t* k16 = q16 + 2 * plane;
+  uint16_t* vt16 = reinterpret_cast<uint16_t*>(b.vt);
   {
     GemmProblem g;
     set_a(g, f_qkv, b.pair_a, w.qkv_w_pair, w.qkv_w_f16, w.qkv_acc_scale);
@@ -684,21 +737,42 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
     g.N = 3 * D;
     g.Kp = D;
     g.epi.bias = w.qkv_b;
-    g.epi.mode = kModeQKVAttn;
-    g.epi.out_pair = b.qk;
-    g.epi.ldp = 2 * D;
-    g.epi.pair_plane = M * 2 * D;
     g.epi.e_split = D;
     g.epi.T = d.T;
-    g.epi.T4 = (d.T + 3) / 4 * 4;
-    g.epi.vt_pair = b.vt;
-    g.epi.vt_plane = static_cast<int64_t>(vt_pair_floats(batch, d.T, p->num_heads) / 2);
+    if (w.attn_f16) {
+      g.epi.mode = kModeQKVAttn16;
+      g.epi.q16 = q16;
+      g.epi.k16 = k16;
+      g.epi.vt16 = vt16;
+      g.epi.vt16_plane = static_cast<int64_t>(vt16_halves(batch, d.T, p->num_heads) / 3);
+      g.epi.T4 = T8;
+      g.epi.q_scale = w.q_scale;
+      g.epi.k_scale = w.k_scale;
+      g.epi.v_scale = w.v_scale;
+    } else {
+      g.epi.mode = kModeQKVAttn;
+      g.epi.out_pair = b.qk;
+      g.epi.ldp = 2 * D;
+      g.epi.pair_plane = M * 2 * D;
+      g.epi.T4 = (d.T + 3) / 4 * 4;
+      g.epi.vt_pair = b.vt;
+      g.epi.vt_plane = static_cast<int64_t>(vt_pair_floats(batch, d.T, p->num_heads) / 2);
+    }
     if (int st = gemm_pairs_launch(g, s)) return st;
   }
-  if (int st = attention_launch(b.qk, 2 * D, 0, b.qk, 2 * D, D, b.vt, nullptr, 0,
-                                f_proj ? nullptr : b.pair_a, D, plane, batch, d.T, p->num_heads,
-                                p->attn_scale, s, f_proj ? a16 : nullptr, D, plane))
+  if (w.attn_f16) {
+    if (int st = attention_f16_launch(q16, k16, D, vt16, T8, nullptr, 0,
+                                      f_proj ? nullptr : b.pair_a, D, plane,
+                                      f_proj ? a16 : nullptr, D, plane, batch, d.T,
+                                      p->num_heads, p->attn_scale, w.q_scale, w.k_scale,
+                                      w.v_scale, s))
+      return st;
+  } else if (int st = attention_launch(b.qk, 2 * D, 0, b.qk, 2 * D, D, b.vt, nullptr, 0,
+                                       f_proj ? nullptr : b.pair_a, D, plane, batch, d.T,
+                                       p->num_heads, p->attn_scale, s, f_proj ? a16 : nullptr, D,
+                                       plane)) {
     return st;
+  }
   {
     GemmProblem g;
     set_a(g, f_proj, b.pair_a, w.proj_w_pair, w.proj_w_f16, w.proj_acc_scale);

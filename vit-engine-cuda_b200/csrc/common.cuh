@@ -306,6 +306,19 @@ __device__ __forceinline__ void umma_tf32_tmem_a(uint32_t d_tmem, uint32_t a_tme
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16 (both f16), one CTA. A (M x K)
+// is read from TMEM: lane = row, two consecutive K elements per 32-bit column
+// (element k in the low half), so one MMA's K = 16 spans 8 columns.
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns from registers: thread i writes lane (base+i).
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(

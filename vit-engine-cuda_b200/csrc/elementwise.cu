@@ -72,6 +72,8 @@ __global__ void split_f16_kernel(const float* __restrict__ x, int64_t rows, int 
   const int64_t o_per_row = ldo / 8;
   const int64_t total = rows * o_per_row;
   const int64_t plane = rows * ldo;
+  // hi * 2^11 (the third plane) is finite only for |hi| < 32.
+  const float limit = nplanes == 3 ? 16.f : kH16Limit;
   bool bad = false;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -86,7 +88,7 @@ __global__ void split_f16_kernel(const float* __restrict__ x, int64_t rows, int 
       for (int u = 0; u < 2; ++u) {
         const int c = c0 + 2 * t + u;
         const float v = (c < cols) ? __fmul_rn(src[2 * t + u], scale) : 0.f;
-        bad |= !(fabsf(v) < kH16Limit);
+        bad |= !(fabsf(v) < limit);
         h16_split(v, h[u], l[u]);
         s[u] = __float2half_rn(__fmul_rn(__half2float(h[u]), kH16LoScale));
       }
@@ -394,6 +396,55 @@ int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int head
   const int64_t plane = static_cast<int64_t>(B) * heads * 64 * T4;
   dim3 grid((T + 31) / 32, 2, B * heads);
   split_transpose_v_kernel<<<grid, dim3(32, 8), 0, s>>>(v, ldv, T, heads, T4, vt_pair, plane);
+  count_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+// v[B*T][ldv] * scale -> vt16[3][B*heads][64][T8]: per (image, head) the
+// transposed FP16 split planes hi, lo*2^11, hi*2^11 (the FP16 attention's V^T
+// operand). Same 32x32 shared-memory transpose as the TF32 version.
+__global__ void split_transpose_v_f16_kernel(const float* __restrict__ v, int64_t ldv, int T,
+                                             int heads, int T8, float scale,
+                                             uint16_t* __restrict__ vt, int64_t plane, int* err) {
+  __shared__ float tile[32][33];
+  const int bh = blockIdx.z;
+  const int b = bh / heads, h = bh - (bh / heads) * heads;
+  const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int k = ty; k < 32; k += 8) {
+    const int t = t0 + k;
+    tile[k][tx] = (t < T) ? v[(static_cast<int64_t>(b) * T + t) * ldv + h * 64 + d0 + tx] : 0.f;
+  }
+  __syncthreads();
+  bool bad = false;
+  for (int k = ty; k < 32; k += 8) {
+    const int t = t0 + tx;
+    if (t < T) {
+      const float x = __fmul_rn(tile[tx][k], scale);
+      bad |= !(fabsf(x) < 16.f);
+      __half hi, lo;
+      h16_split(x, hi, lo);
+      const int64_t idx = (static_cast<int64_t>(bh) * 64 + d0 + k) * T8 + t;
+      vt[idx] = __half_as_ushort(hi);
+      vt[idx + plane] = __half_as_ushort(lo);
+      vt[idx + 2 * plane] = __half_as_ushort(__float2half_rn(__half2float(hi) * kH16LoScale));
+    }
+  }
+  if (bad) report_error(err, kErrF16Range);
+}
+
+int split_transpose_v_f16_launch(const float* v, int64_t ldv, int B, int T, int heads, float scale,
+                                 uint16_t* vt16, cudaStream_t s) {
+  if (!v || !vt16 || B < 0 || T < 0 || heads <= 0 || ldv < heads * 64 || !(scale > 0.f))
+    return VITB200_E_INVALID_ARG;
+  if (B == 0 || T == 0) return 0;
+  int* err = device_error_word();
+  if (err == nullptr) return VITB200_E_INVALID_ARG;
+  const int T8 = (T + 7) / 8 * 8;
+  const int64_t plane = static_cast<int64_t>(B) * heads * 64 * T8;
+  dim3 grid((T + 31) / 32, 2, B * heads);
+  split_transpose_v_f16_kernel<<<grid, dim3(32, 8), 0, s>>>(v, ldv, T, heads, T8, scale, vt16,
+                                                            plane, err);
   count_launch();
   return cuda_status(cudaGetLastError());
 }

@@ -109,6 +109,64 @@ struct GemmCfg {
 // Row-contiguous outputs go through the warp's transpose buffer `stg`, so every
 // global access instruction covers four whole 128-byte row segments instead of
 // sixteen bytes of 32 different rows.
+// Stores the FP16 split of a warp's 32 x 32 slab (lane i = row m_base + i,
+// values v) as planes base[p * plane + row * ld + col_base ..]: hi, lo * 2^11
+// and, with `third`, hi * 2^11. Through the warp's transpose buffer: words
+// 0-15 of a row hold hi halves, 16-31 lo halves; lanes 0-3 of each group of
+// eight store a row's hi (64 B), lanes 4-7 its lo, four rows per instruction.
+__device__ __forceinline__ void h16_slab_store(const float (&v)[32], float* stg, int lane,
+                                               int64_t m_base, int64_t M, uint16_t* base,
+                                               int64_t ld, int64_t plane, int64_t col_base,
+                                               bool third) {
+  const int rsub = lane >> 3;
+  const int c4 = (lane & 7) * 4;
+  float* my_row = stg + lane * kStgPitch;
+  uint32_t sw[16];
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      __half h0, l0, h1, l1;
+      h16_split(v[j + 2 * t], h0, l0);
+      h16_split(v[j + 2 * t + 1], h1, l1);
+      hw[t] = pack_h2(h0, h1);
+      lw[t] = pack_h2(l0, l1);
+      sw[j / 2 + t] = pack_h2(__float2half_rn(__half2float(h0) * kH16LoScale),
+                              __float2half_rn(__half2float(h1) * kH16LoScale));
+    }
+    *reinterpret_cast<uint4*>(my_row + j / 2) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(my_row + 16 + j / 2) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+  __syncwarp();
+  const int pl = c4 >> 4;          // 0: hi, 1: lo
+  const int hcol = (c4 & 15) * 2;  // first of this lane's eight columns
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = 4 * k + rsub;
+    const int64_t mr = m_base + r;
+    const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgPitch + c4);
+    if (mr < M) *reinterpret_cast<uint4*>(base + pl * plane + mr * ld + col_base + hcol) = t;
+  }
+  __syncwarp();
+  if (third) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 4)
+      *reinterpret_cast<uint4*>(my_row + j) = make_uint4(sw[j], sw[j + 1], sw[j + 2], sw[j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + rsub;
+      const int64_t mr = m_base + r;
+      if (c4 < 16 && mr < M) {
+        const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgPitch + c4);
+        *reinterpret_cast<uint4*>(base + 2 * plane + mr * ld + col_base + hcol) = t;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <bool F16>
 __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base, int lane, int n0,
                                               float (&v)[32], float* stg) {
@@ -134,6 +192,38 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
   if (e.gelu) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+  }
+
+  if (e.mode == kModeQKVAttn16) {
+    // q | k | v column thirds (E % 64 == 0: slabs are full and never straddle).
+    const int E = e.e_split;
+    const int part = n0 / E;
+    const float sc = part == 0 ? e.q_scale : (part == 1 ? e.k_scale : e.v_scale);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = v[j] * sc;  // exact: a power of two
+    if (part < 2) {
+      h16_slab_store(v, stg, lane, m_base, a.M, part == 0 ? e.q16 : e.k16, E, a.M * E,
+                     n0 - part * E, part == 1);
+      return;
+    }
+    // V: transposed per (image, head); lanes hold consecutive tokens, so each
+    // column's store is one contiguous 64-byte run per plane.
+    if (!row_ok) return;
+    const int vc = n0 - 2 * E;
+    const int64_t bimg = m / e.T;
+    const int64_t t = m - bimg * e.T;
+    const int64_t head_row = (bimg * (E / 64) + vc / 64) * 64 + (vc & 63);
+    __half* dst = reinterpret_cast<__half*>(e.vt16) + head_row * e.T4 + t;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      __half hi, lo;
+      h16_split(v[j], hi, lo);
+      const int64_t o = static_cast<int64_t>(j) * e.T4;
+      dst[o] = hi;
+      dst[o + e.vt16_plane] = lo;
+      dst[o + 2 * e.vt16_plane] = __float2half_rn(__half2float(hi) * kH16LoScale);
+    }
+    return;
   }
 
   if (e.mode == kModeQKVAttn && n0 >= 2 * e.e_split) {
@@ -227,38 +317,8 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
       }
       flush(e.out_pair + e.pair_plane, e.ldp);
     }
-    if (e.out_h16 != nullptr) {
-      // Row buffer: words 0-15 = hi halves of the 32 columns, 16-31 = lo
-      // halves. Lanes 0-3 of each group of eight store a row's hi (64 B),
-      // lanes 4-7 its lo, four rows per instruction.
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          __half h0, l0, h1, l1;
-          h16_split(v[j + 2 * t], h0, l0);
-          h16_split(v[j + 2 * t + 1], h1, l1);
-          hw[t] = pack_h2(h0, h1);
-          lw[t] = pack_h2(l0, l1);
-        }
-        *reinterpret_cast<uint4*>(my_row + j / 2) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(my_row + 16 + j / 2) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      }
-      __syncwarp();
-      const int plane = c4 >> 4;     // 0: hi, 1: lo
-      const int hcol = (c4 & 15) * 2;  // first of this lane's eight columns
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = 4 * k + rsub;
-        const int64_t mr = m_base + r;
-        const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgPitch + c4);
-        if (mr < a.M)
-          *reinterpret_cast<uint4*>(e.out_h16 + plane * e.h16_plane + mr * e.ldh + col_base +
-                                    hcol) = t;
-      }
-      __syncwarp();
-    }
+    if (e.out_h16 != nullptr)
+      h16_slab_store(v, stg, lane, m_base, a.M, e.out_h16, e.ldh, e.h16_plane, col_base, false);
     return;
   }
 
@@ -855,7 +915,8 @@ int gemm_prepare_device() {
 int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
   const bool f16 = p.f16 != 0;
   if (p.M < 0 || p.N < 0 || p.Kp < 0 || (p.Kp % (f16 ? 8 : 4)) != 0) return VITB200_E_INVALID_ARG;
-  if (p.epi.out == nullptr && p.epi.out_pair == nullptr && p.epi.out_h16 == nullptr)
+  if (p.epi.out == nullptr && p.epi.out_pair == nullptr && p.epi.out_h16 == nullptr &&
+      p.epi.mode != kModeQKVAttn16)
     return VITB200_E_INVALID_ARG;
   if (p.M == 0 || p.N == 0) return 0;
   if (p.epi.mode == kModeSplit3 && (p.epi.e_split <= 0 || p.epi.e_split % 32 != 0))
@@ -866,6 +927,12 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
        p.epi.T4 < p.epi.T || p.epi.ldp != 2 * p.epi.e_split))
     return VITB200_E_INVALID_ARG;
   if (p.epi.mode == kModePatch && (p.epi.P <= 0 || p.epi.T != p.epi.P + 1 || !p.epi.pos))
+    return VITB200_E_INVALID_ARG;
+  if (p.epi.mode == kModeQKVAttn16 &&
+      (p.epi.e_split <= 0 || p.epi.e_split % 64 != 0 || p.N != 3 * p.epi.e_split ||
+       !p.epi.q16 || !p.epi.k16 || !p.epi.vt16 || p.epi.out || p.epi.out_pair || p.epi.out_h16 ||
+       p.epi.residual || p.epi.gelu || p.epi.T <= 0 || p.epi.T4 < p.epi.T || p.epi.T4 % 8 ||
+       reinterpret_cast<uintptr_t>(p.epi.q16) % 16 || reinterpret_cast<uintptr_t>(p.epi.k16) % 16))
     return VITB200_E_INVALID_ARG;
   if (p.Kp == 0) return gemm_k0_launch(p, s);
   const void* a_ptr = f16 ? static_cast<const void*>(p.a_h16) : p.a_pair;

@@ -42,7 +42,8 @@ class BlockParams(ctypes.Structure):
         ("qkv_w_f16", c_void_p), ("qkv_acc_scale", c_float),
         ("proj_w_f16", c_void_p), ("proj_acc_scale", c_float),
         ("fc1_w_f16", c_void_p), ("fc1_acc_scale", c_float),
-        ("fc2_w_f16", c_void_p), ("fc2_acc_scale", c_float)]
+        ("fc2_w_f16", c_void_p), ("fc2_acc_scale", c_float),
+        ("attn_f16", c_int), ("q_scale", c_float), ("k_scale", c_float), ("v_scale", c_float)]
 
 
 class VitParams(ctypes.Structure):
@@ -84,6 +85,10 @@ _SIGNATURES = {
     "vitb200_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "vitb200_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int64, c_int64, c_int64,
                                   c_int64, c_float, _P, c_size_t, _P]),
+    "vitb200_attention_f16_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "vitb200_attention_f16": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int64, c_int64,
+                                      c_int64, c_int64, c_float, c_float, c_float, _P, c_size_t,
+                                      _P]),
     "vitb200_patch_embed_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "vitb200_patch_embed": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P,
                                     c_size_t, _P]),

@@ -29,7 +29,8 @@ import torch.nn as nn
 
 from . import _C, _lib
 from ._lib import BlockParams, VitParams, lib
-from .split import F16_SAFE_BOUND, block_input_bounds, f16_weight, f16_weight_ok
+from .split import (F16_SAFE_BOUND, block_input_bounds, f16_weight, f16_weight_ok,
+                    operand_scale)
 
 _BLOCK_KEYS = [
     ("norm1_gamma", "norm1.weight"), ("norm1_beta", "norm1.bias"),
@@ -162,6 +163,13 @@ class ViTCUDA(nn.Module):
                         w[name] = (_split_pair(weight), None, 0.0)
                         kinds[name] = "tf32"
                     keep += [t for t in w[name][:2] if t is not None]
+                # The FP16 attention: |q| within the split's range, k and v
+                # scaled by powers of two into |x| <= 8 (their third plane
+                # hi * 2^11 must stay finite).
+                k_s, v_s = operand_scale(bounds["k"]), operand_scale(bounds["v"])
+                attn_f16 = (self.operands == "auto" and bounds["q"] < F16_SAFE_BOUND
+                            and k_s is not None and v_s is not None)
+                kinds["attn"] = "f16" if attn_f16 else "tf32"
                 self.gemm_operands.append(kinds)
                 vecs = [blk.norm1_gamma, blk.norm1_beta, blk.qkv_bias, blk.proj_bias,
                         blk.norm2_gamma, blk.norm2_beta, blk.fc1_bias, blk.fc2_bias]
@@ -173,7 +181,9 @@ class ViTCUDA(nn.Module):
                     ptr(w["proj"][0]), vecs[3].data_ptr(), vecs[4].data_ptr(), vecs[5].data_ptr(),
                     ptr(w["fc1"][0]), vecs[6].data_ptr(), ptr(w["fc2"][0]), vecs[7].data_ptr(),
                     ptr(w["qkv"][1]), w["qkv"][2], ptr(w["proj"][1]), w["proj"][2],
-                    ptr(w["fc1"][1]), w["fc1"][2], ptr(w["fc2"][1]), w["fc2"][2])
+                    ptr(w["fc1"][1]), w["fc1"][2], ptr(w["fc2"][1]), w["fc2"][2],
+                    1 if attn_f16 else 0, 1.0, k_s if attn_f16 else 1.0,
+                    v_s if attn_f16 else 1.0)
             vecs = {n: getattr(self, n).contiguous() for n in
                     ("patch_bias", "cls_token", "pos_embed", "norm_gamma", "norm_beta",
                      "head_bias")}

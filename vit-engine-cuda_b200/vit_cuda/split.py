@@ -82,15 +82,27 @@ def linear_bound(in_bound: float, w: torch.Tensor, b: torch.Tensor | None) -> fl
 
 
 def block_input_bounds(blk, embed_dim: int) -> dict[str, float]:
-    """A-operand magnitude bounds of one encoder block's four GEMMs: qkv and
-    fc1 take LayerNorm outputs; proj takes attention outputs, convex
-    combinations of V rows; fc2 takes GELU(fc1 output), at most max(|h|, 0.17)."""
+    """Magnitude bounds of one encoder block's split operands: qkv and fc1
+    take LayerNorm outputs; q, k, v (the attention's operands) are linear maps
+    of LN1's output; proj takes attention outputs, convex combinations of V
+    rows; fc2 takes GELU(fc1 output), at most max(|h|, 0.17)."""
     ln1 = layernorm_bound(blk.norm1_gamma, blk.norm1_beta)
     ln2 = layernorm_bound(blk.norm2_gamma, blk.norm2_beta)
-    v_rows = slice(2 * embed_dim, 3 * embed_dim)
-    v = linear_bound(ln1, blk.qkv_weight[v_rows], blk.qkv_bias[v_rows])
+    E = embed_dim
+    q = linear_bound(ln1, blk.qkv_weight[:E], blk.qkv_bias[:E])
+    k = linear_bound(ln1, blk.qkv_weight[E:2 * E], blk.qkv_bias[E:2 * E])
+    v = linear_bound(ln1, blk.qkv_weight[2 * E:3 * E], blk.qkv_bias[2 * E:3 * E])
     h = linear_bound(ln2, blk.fc1_weight, blk.fc1_bias)
-    return {"qkv": ln1, "proj": v, "fc1": ln2, "fc2": max(h, 0.2)}
+    return {"qkv": ln1, "proj": v, "fc1": ln2, "fc2": max(h, 0.2), "q": q, "k": k, "v": v}
+
+
+def operand_scale(bound: float, target: float = 8.0) -> float | None:
+    """Power of two s with bound * s <= target (None when the bound is not a
+    finite positive number or s would leave [2^-60, 2^60])."""
+    if not (math.isfinite(bound) and bound > 0.0):
+        return None
+    s = 2.0 ** math.floor(math.log2(target / bound))
+    return s if 2.0 ** -60 <= s <= 2.0 ** 60 else None
 
 
 def f16_weight_ok(w: torch.Tensor) -> bool:
