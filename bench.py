@@ -57,6 +57,9 @@ CONFIGS = {
     "bs512_384": (512, 384),   # BASELINE configs[4] per-GPU shard (B=4096 over 8 GPUs)
 }
 GFLOP_PER_IMG = {224: 35.1277, 384: 110.9687}
+# Block GEMMs as the model launches them: (N, K, epilogue, FP16-split output).
+ROOFLINE_GEMMS = {"qkv": (2304, 768, "bias", False), "proj": (768, 768, "resid", False),
+                  "fc1": (3072, 768, "gelu", True), "fc2": (768, 3072, "resid", False)}
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -75,6 +78,8 @@ def parse_args():
     ap.add_argument("--mode", choices=["full", "roofline"], default="full",
                     help="roofline: time only the dominant GEMM launch (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None, help="override images per GPU")
+    ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS), default="fc1",
+                    help="roofline mode: which block GEMM to time")
     return ap.parse_args()
 
 
@@ -160,12 +165,15 @@ def timed(fn, steps, world, dev):
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
-def gemm_roofline(dev, M: int, N: int, K: int, reps: int = 10):
-    """Times the fc1 GEMM as the model launches it (FP16-split operands, bias +
-    GELU, FP16-split output) alone; returns ms per launch."""
+def gemm_roofline(dev, M: int, name: str = "fc1", reps: int = 10):
+    """Times one block GEMM as the model launches it (FP16-split operands; fc1:
+    bias + GELU with FP16-split output; proj / fc2: bias + residual; qkv: bias)
+    alone; returns ms per launch."""
     from vit_cuda import _lib
     from vit_cuda.split import f16_planes, f16_weight
     lib = _lib.lib
+    N, K, epi, split_out = ROOFLINE_GEMMS[name]
+    code = {"bias": _lib.EPI_BIAS, "gelu": _lib.EPI_BIAS_GELU, "resid": _lib.EPI_BIAS_RESID}[epi]
     s = torch.cuda.current_stream().cuda_stream
     a = torch.randn(M, K, device=dev)
     w = torch.randn(N, K, device=dev) * 0.02
@@ -173,12 +181,15 @@ def gemm_roofline(dev, M: int, N: int, K: int, reps: int = 10):
     ap = f16_planes(a, 2)
     wp, acc_scale = f16_weight(w)
     del a
-    out = torch.empty(2, M, N, dtype=torch.int16, device=dev)
+    out = torch.empty(2, M, N, dtype=torch.int16, device=dev) if split_out else None
+    y = None if split_out else torch.randn(M, N, device=dev)
 
     def launch():
         _lib.check(lib.vitb200_gemm_f16(ap.data_ptr(), wp.data_ptr(), acc_scale, bias.data_ptr(),
-                                        None, None, 0, out.data_ptr(), M, K, N,
-                                        _lib.EPI_BIAS_GELU, s), "gemm")
+                                        y.data_ptr() if epi == "resid" else None,
+                                        y.data_ptr() if y is not None else None, N,
+                                        out.data_ptr() if out is not None else None, M, K, N,
+                                        code, s), "gemm")
 
     for _ in range(3):
         launch()
@@ -190,7 +201,7 @@ def gemm_roofline(dev, M: int, N: int, K: int, reps: int = 10):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    del ap, wp, out
+    del ap, wp, out, y
     return ms
 
 
@@ -348,7 +359,7 @@ def run_ours(args):
 
     # Roofline of the fc1 GEMM (FP16-split operands), the model's largest GEMM.
     M = batch * T
-    gemm_ms = gemm_roofline(dev, M, 3072, 768)
+    gemm_ms = gemm_roofline(dev, M, "fc1")
     alg_flops = 2.0 * M * 3072 * 768
     peak, peak_src = measured_tensor_peak()
     achieved = 3 * alg_flops / (gemm_ms * 1e-3) / 1e12
@@ -437,9 +448,10 @@ def run_roofline_only(args):
     if args.batch:
         batch = args.batch
     M = batch * ((img // 16) ** 2 + 1)
-    ms = gemm_roofline(dev, M, 3072, 768, reps=max(1, args.steps))
-    emit({"mode": "roofline", "kernel": "gemm f16x3 fc1", "M": M, "N": 3072, "K": 768,
-          "kernel_ms": ms, "f16_pipe_tflops": 3 * 2.0 * M * 3072 * 768 / (ms * 1e-3) / 1e12})
+    N, K = ROOFLINE_GEMMS[args.kernel][:2]
+    ms = gemm_roofline(dev, M, args.kernel, reps=max(1, args.steps))
+    emit({"mode": "roofline", "kernel": f"gemm f16x3 {args.kernel}", "M": M, "N": N, "K": K,
+          "kernel_ms": ms, "f16_pipe_tflops": 3 * 2.0 * M * N * K / (ms * 1e-3) / 1e12})
 
 
 def main():

@@ -76,14 +76,16 @@ int vitb200_num_sms(void);
  * streams; a CUDA-graph replay issues none). For benchmarks and tests. */
 uint64_t vitb200_launch_count(void);
 
-/* GEMM tile configuration: 0 = automatic (default); 1..12 force one of the
+/* GEMM tile configuration: 0 = automatic (default); 1..15 force one of the
  * compiled configurations. On TF32 pairs: 1 = 128x128 tiles, 2 stages of K=32;
  * 2 = 128x128, 5 stages of K=16; 3 = 128x64, 3 stages of K=32; 4 = as 1 with K
  * chunks of 64; 5 = 128x256, 3 stages of K=16; 6 = 256x256 on a CTA pair, 2
  * stages of K=32; 7 = 256x256 pair, 5 stages of K=16; 8 = as 7 with K chunks of
  * 256. On FP16 splits (vitb200_gemm_f16 and the model's F16 path): 9 = 256x256
  * pair, 2 stages of K=64; 10 = 128x128, 2 stages of K=64; 11 = 128x64, 3
- * stages of K=64; 12 = 256x256 pair, 4 stages of K=32. A forced configuration
+ * stages of K=64; 12 = 256x256 pair, 4 stages of K=32; 13, 14 = as 9, 10 with
+ * two W planes (cross products folded in by tcgen05.mma's scale-input-d, K
+ * chunks of 64); 15 = as 9 with K chunks of 256. A forced configuration
  * of the other operand kind is ignored. All accumulate K in chunks (128 unless
  * stated) on the tensor core and sum the chunks in FP32 registers. Returns the
  * previous setting. For tuning and tests; process-wide. */

@@ -88,7 +88,7 @@ def test_gemm_f16_multi_tile(vlib, cuda, shape, epi):
     check_fp32_parity(y, x, w, bias, res, epi)
 
 
-@pytest.mark.parametrize("variant", [9, 10, 11, 12])
+@pytest.mark.parametrize("variant", [9, 10, 11, 12, 13, 14, 15])
 @pytest.mark.parametrize("shape", [(394, 768, 2304), (200, 3072, 768), (130, 96, 520),
                                    (2100, 300, 1300)])
 def test_gemm_f16_variants(vlib, cuda, variant, shape):

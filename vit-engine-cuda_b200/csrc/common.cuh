@@ -74,6 +74,18 @@ __device__ __forceinline__ void h16_split(float x, __half& hi, __half& lo) {
   lo = __float2half_rn(__fmul_rn(__fsub_rn(x, __half2float(hi)), kH16LoScale));
 }
 
+// The FP16 splits of two values at once, packed as they are stored (a in the
+// low half, b in the high half): same rounding as h16_split, with the paired
+// f32 -> f16x2 conversions.
+__device__ __forceinline__ void h16_split2(float a, float b, uint32_t& hi2, uint32_t& lo2) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(__fmul_rn(__fsub_rn(a, hf.x), kH16LoScale),
+                                      __fmul_rn(__fsub_rn(b, hf.y), kH16LoScale));
+  hi2 = *reinterpret_cast<const uint32_t*>(&h);
+  lo2 = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 // Two halves packed little-endian (column c in the low half, c+1 in the high).
 __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
   return static_cast<uint32_t>(__half_as_ushort(a)) |
@@ -197,6 +209,28 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] = A * B + D * 2^-11 (tcgen05.mma's scale-input-d): folds a product
+// into an accumulator that so far holds values scaled by 2^11. kind::f16,
+// operands in shared memory; one CTA, or a CTA pair.
+__device__ __forceinline__ void umma_f16_sd11(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p, 11;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair_sd11(uint32_t d_tmem, uint64_t a_desc,
+                                                   uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p, 11;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
       : "memory");
 }
 

@@ -50,6 +50,7 @@ struct GemmArgs {
   int vec_pair;    // pair rows are 16-byte aligned
   int vec_res;     // residual rows are 16-byte aligned
   int vec_h16;     // FP16-pair rows are 16-byte aligned
+  int vec_bias;    // bias is 16-byte aligned
   float acc_scale; // F16 kernels: multiplies the accumulator (a power of two)
   int* err;
   GemmEpilogue epi;
@@ -69,8 +70,16 @@ constexpr uint32_t kEpiRegs = 224;
 static_assert(128 * kCtrlRegs + 256 * kEpiRegs == 384 * 168, "register split");
 constexpr int kTmemAll = 512;  // TMEM columns: chunk accumulators of BN columns each
 
-template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+// Operand kinds: TF32 pairs; FP16 splits with B's third plane hi*2^11 (one
+// accumulator takes all three products); FP16 splits with two B planes, the
+// cross products accumulated first and folded in by scale-input-d (every
+// stage is one chunk).
+enum OperandKind : int { kKindTF32 = 0, kKindF16 = 1, kKindF16SD = 2 };
+
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 struct GemmCfg {
+  static constexpr bool F16 = KIND != kKindTF32;
+  static constexpr bool SD = KIND == kKindF16SD;
   // PAIR: the two CTAs of a cluster share a 256 x BN tile; each holds 128 rows
   // of A, BN/2 rows of B and 128 x BN accumulators in its own TMEM.
   // F16: operands are FP16 splits (A: hi, lo; B: hi, lo, hi*2^11), TF32
@@ -78,7 +87,7 @@ struct GemmCfg {
   static constexpr int kEs = F16 ? 2 : 4;       // bytes per element
   static constexpr int kRowBytes = BK * kEs;    // one K-major tile row
   static constexpr int kMmaK = F16 ? 16 : 8;    // K per tcgen05.mma (32 bytes)
-  static constexpr int kBPlanes = F16 ? 3 : 2;
+  static constexpr int kBPlanes = KIND == kKindF16 ? 3 : 2;
   static constexpr int kBRows = PAIR ? BN / 2 : BN;
   static constexpr int kAPlane = kBM * BK * kEs;  // bytes of one A plane
   static constexpr int kBPlane = kBRows * BK * kEs;
@@ -99,6 +108,7 @@ struct GemmCfg {
                 "TMEM columns must be a power of two in [32, 512]");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
   static_assert(CHUNK_KB >= 1, "chunk");
+  static_assert(!SD || CHUNK_KB == 1, "scale-input-d needs one stage per chunk");
 };
 
 // Epilogue of one 32 x 32 slab, warp-collective: lane i holds row m_base + i,
@@ -127,13 +137,12 @@ __device__ __forceinline__ void h16_slab_store(const float (&v)[32], float* stg,
     uint32_t hw[4], lw[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      __half h0, l0, h1, l1;
-      h16_split(v[j + 2 * t], h0, l0);
-      h16_split(v[j + 2 * t + 1], h1, l1);
-      hw[t] = pack_h2(h0, h1);
-      lw[t] = pack_h2(l0, l1);
-      sw[j / 2 + t] = pack_h2(__float2half_rn(__half2float(h0) * kH16LoScale),
-                              __float2half_rn(__half2float(h1) * kH16LoScale));
+      h16_split2(v[j + 2 * t], v[j + 2 * t + 1], hw[t], lw[t]);
+      if (third) {
+        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[t]));
+        const __half2 s2 = __floats2half2_rn(hf.x * kH16LoScale, hf.y * kH16LoScale);
+        sw[j / 2 + t] = *reinterpret_cast<const uint32_t*>(&s2);
+      }
     }
     *reinterpret_cast<uint4*>(my_row + j / 2) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     *reinterpret_cast<uint4*>(my_row + 16 + j / 2) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
@@ -183,10 +192,21 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
   }
 
   if (e.bias != nullptr) {
+    if (full && a.vec_bias) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = n0 + j;
-      v[j] = v[j] + ((n < N) ? __ldg(e.bias + n) : 0.f);
+      for (int j = 0; j < 32; j += 4) {
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(e.bias + n0 + j));
+        v[j] = v[j] + b4.x;
+        v[j + 1] = v[j + 1] + b4.y;
+        v[j + 2] = v[j + 2] + b4.z;
+        v[j + 3] = v[j + 3] + b4.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = n0 + j;
+        v[j] = v[j] + ((n < N) ? __ldg(e.bias + n) : 0.f);
+      }
     }
   }
   if (e.gelu) {
@@ -410,11 +430,12 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
   }
 }
 
-template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
-  using Cfg = GemmCfg<F16, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  constexpr bool F16 = Cfg::F16;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -565,8 +586,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_lo = a_hi + Cfg::kAPlane;
           const uint32_t b_hi = a_hi + 2 * Cfg::kAPlane;
           const uint32_t b_lo = b_hi + Cfg::kBPlane;
-          // hi * hi: TF32 uses B's hi plane; F16 its third plane, hi * 2^11.
-          const uint32_t b_hh = F16 ? b_hi + 2 * Cfg::kBPlane : b_hi;
+          // hi * hi: TF32 and scale-input-d use B's hi plane; F16 its third
+          // plane, hi * 2^11.
+          const uint32_t b_hh = KIND == kKindF16 ? b_hi + 2 * Cfg::kBPlane : b_hi;
           auto mma = [&](uint64_t da, uint64_t db, uint32_t acc) {
             if constexpr (F16 && PAIR) {
               umma_f16_pair(d_tmem, da, db, Cfg::kIdesc, acc);
@@ -578,18 +600,48 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_tf32(d_tmem, da, db, Cfg::kIdesc, acc);
             }
           };
+          if constexpr (Cfg::SD) {
+            // The stage's cross products (each scaled by 2^11) first, then
+            // hi * hi with the accumulator scaled by 2^-11 on the first one.
 #pragma unroll
-          for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
-            const uint32_t koff = static_cast<uint32_t>(kk * 32);  // one MMA's K = 32 bytes
-            const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
-            const uint64_t dal = make_sdesc_kmajor(a_lo + koff, Cfg::kRowBytes);
-            const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
-            const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, Cfg::kRowBytes);
-            const uint64_t dbhh = make_sdesc_kmajor(b_hh + koff, Cfg::kRowBytes);
-            const uint32_t acc0 = (chunk_first && kk == 0) ? 0u : 1u;
-            mma(dal, dbh, acc0);  // lo * hi
-            mma(dah, dbl, 1u);    // hi * lo
-            mma(dah, dbhh, 1u);   // hi * hi
+            for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+              const uint32_t koff = static_cast<uint32_t>(kk * 32);
+              const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
+              const uint64_t dal = make_sdesc_kmajor(a_lo + koff, Cfg::kRowBytes);
+              const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
+              const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, Cfg::kRowBytes);
+              mma(dal, dbh, kk == 0 ? 0u : 1u);  // lo * hi
+              mma(dah, dbl, 1u);                 // hi * lo
+            }
+#pragma unroll
+            for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+              const uint32_t koff = static_cast<uint32_t>(kk * 32);
+              const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
+              const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
+              if (kk == 0) {
+                if constexpr (PAIR) {
+                  umma_f16_pair_sd11(d_tmem, dah, dbh, Cfg::kIdesc);
+                } else {
+                  umma_f16_sd11(d_tmem, dah, dbh, Cfg::kIdesc);
+                }
+              } else {
+                mma(dah, dbh, 1u);  // hi * hi
+              }
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+              const uint32_t koff = static_cast<uint32_t>(kk * 32);  // one MMA's K = 32 bytes
+              const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
+              const uint64_t dal = make_sdesc_kmajor(a_lo + koff, Cfg::kRowBytes);
+              const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
+              const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, Cfg::kRowBytes);
+              const uint64_t dbhh = make_sdesc_kmajor(b_hh + koff, Cfg::kRowBytes);
+              const uint32_t acc0 = (chunk_first && kk == 0) ? 0u : 1u;
+              mma(dal, dbh, acc0);  // lo * hi
+              mma(dah, dbl, 1u);    // hi * lo
+              mma(dah, dbhh, 1u);   // hi * hi
+            }
           }
           commit(&empty_bar[stage]);  // frees the stage once these MMAs finish
           if (++stage == STAGES) {
@@ -766,30 +818,33 @@ struct Variant {
   int f16, bn, bk, stages, chunk_kb, pair;
 };
 // Index 1.. are selectable with gemm_set_variant; 0 = automatic. 1-8 take TF32
-// pairs, 9-12 FP16 splits; a forced variant of the other operand kind is ignored.
+// pairs, 9-14 FP16 splits (13, 14: two B planes with scale-input-d); a forced
+// variant of the other operand kind is ignored.
 constexpr Variant kVariants[] = {
     {0, 0, 0, 0, 0, 0},     {0, 128, 32, 2, 4, 0}, {0, 128, 16, 5, 8, 0}, {0, 64, 32, 3, 4, 0},
     {0, 128, 32, 2, 2, 0},  {0, 256, 16, 3, 8, 0}, {0, 256, 32, 2, 4, 1}, {0, 256, 16, 5, 8, 1},
     {0, 256, 16, 5, 16, 1}, {1, 256, 64, 2, 2, 1}, {1, 128, 64, 2, 2, 0}, {1, 64, 64, 3, 2, 0},
-    {1, 256, 32, 4, 4, 1},
+    {1, 256, 32, 4, 4, 1},  {1, 256, 64, 2, 1, 1}, {1, 128, 64, 2, 1, 0}, {1, 256, 64, 2, 4, 1},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 constexpr int kPairVariant = 6;
-constexpr int kF16PairVariant = 9;
+constexpr int kF16PairVariant = 15;
 int g_forced_variant = 0;
 
 // Cluster-of-two slots that fit on the device at once, per device (0 = not
 // queried yet).
 int g_pair_slots[64] = {};
 
-template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
-  using Cfg = GemmCfg<F16, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  constexpr bool F16 = Cfg::F16;
   CUtensorMap ta, tb;
   int st = F16 ? make_planes_map(&ta, p.a_h16, p.M, p.Kp, 2, kBM, BK, 1)
                : make_pair_map(&ta, p.a_pair, p.M, p.Kp, kBM, BK);
   if (st) return st;
-  st = F16 ? make_planes_map(&tb, p.b_h16, p.N, p.Kp, 3, Cfg::kBRows, BK, 1)
+  // Weights hold three planes; scale-input-d reads only the first two.
+  st = F16 ? make_planes_map(&tb, p.b_h16, p.N, p.Kp, Cfg::kBPlanes, Cfg::kBRows, BK, 1)
            : make_pair_map(&tb, p.b_pair, p.N, p.Kp, Cfg::kBRows, BK);
   if (st) return st;
   GemmArgs a;
@@ -812,7 +867,10 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
               (e.ldr % 4 == 0);
   a.vec_h16 = (e.out_h16 != nullptr) && (reinterpret_cast<uintptr_t>(e.out_h16) % 16 == 0) &&
               (e.ldh % 8 == 0) && (e.h16_plane % 8 == 0);
-  a.acc_scale = F16 ? p.acc_scale : 1.f;
+  // The accumulator holds 2^11 * s * (A.B) (three-plane kind) or s * (A.B)
+  // (scale-input-d), s the scale B was split with; p.acc_scale = 2^-11 / s.
+  a.acc_scale = F16 ? (Cfg::SD ? p.acc_scale * kH16LoScale : p.acc_scale) : 1.f;
+  a.vec_bias = (e.bias != nullptr) && (reinterpret_cast<uintptr_t>(e.bias) % 16 == 0);
   a.err = err;
   a.epi = e;
   if constexpr (PAIR) {
@@ -832,7 +890,7 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
     int slots = (dev >= 0 && dev < 64) ? g_pair_slots[dev] : 0;
     if (slots <= 0) {
       cfg.gridDim = dim3(2 * static_cast<unsigned>(device_num_sms() / 2));
-      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>,
+      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>,
                                          &cfg) != cudaSuccess ||
           slots <= 0) {
         (void)cudaGetLastError();
@@ -841,24 +899,24 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
       if (dev >= 0 && dev < 64) g_pair_slots[dev] = slots;
     }
     cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
-    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>,
+    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>,
                                         ta, tb, a));
     count_launch();
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_num_sms()));
-    gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>
+    gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>
         <<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, a);
     count_launch();
     return cuda_status(cudaGetLastError());
   }
 }
 
-template <bool F16, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
 int set_smem_attr() {
-  using Cfg = GemmCfg<F16, BN, BK, STAGES, CHUNK_KB, PAIR>;
-  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<F16, BN, BK, STAGES, CHUNK_KB, PAIR>,
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           Cfg::kSmemBytes));
 }
@@ -896,18 +954,21 @@ int gemm_set_variant(int v) {
 }
 
 int gemm_prepare_device() {
-  int st = set_smem_attr<false, 128, 32, 2, 4, false>();
-  if (!st) st = set_smem_attr<false, 128, 16, 5, 8, false>();
-  if (!st) st = set_smem_attr<false, 64, 32, 3, 4, false>();
-  if (!st) st = set_smem_attr<false, 128, 32, 2, 2, false>();
-  if (!st) st = set_smem_attr<false, 256, 16, 3, 8, false>();
-  if (!st) st = set_smem_attr<false, 256, 32, 2, 4, true>();
-  if (!st) st = set_smem_attr<false, 256, 16, 5, 8, true>();
-  if (!st) st = set_smem_attr<false, 256, 16, 5, 16, true>();
-  if (!st) st = set_smem_attr<true, 256, 64, 2, 2, true>();
-  if (!st) st = set_smem_attr<true, 128, 64, 2, 2, false>();
-  if (!st) st = set_smem_attr<true, 64, 64, 3, 2, false>();
-  if (!st) st = set_smem_attr<true, 256, 32, 4, 4, true>();
+  int st = set_smem_attr<kKindTF32, 128, 32, 2, 4, false>();
+  if (!st) st = set_smem_attr<kKindTF32, 128, 16, 5, 8, false>();
+  if (!st) st = set_smem_attr<kKindTF32, 64, 32, 3, 4, false>();
+  if (!st) st = set_smem_attr<kKindTF32, 128, 32, 2, 2, false>();
+  if (!st) st = set_smem_attr<kKindTF32, 256, 16, 3, 8, false>();
+  if (!st) st = set_smem_attr<kKindTF32, 256, 32, 2, 4, true>();
+  if (!st) st = set_smem_attr<kKindTF32, 256, 16, 5, 8, true>();
+  if (!st) st = set_smem_attr<kKindTF32, 256, 16, 5, 16, true>();
+  if (!st) st = set_smem_attr<kKindF16, 256, 64, 2, 2, true>();
+  if (!st) st = set_smem_attr<kKindF16, 128, 64, 2, 2, false>();
+  if (!st) st = set_smem_attr<kKindF16, 64, 64, 3, 2, false>();
+  if (!st) st = set_smem_attr<kKindF16, 256, 32, 4, 4, true>();
+  if (!st) st = set_smem_attr<kKindF16SD, 256, 64, 2, 1, true>();
+  if (!st) st = set_smem_attr<kKindF16SD, 128, 64, 2, 1, false>();
+  if (!st) st = set_smem_attr<kKindF16, 256, 64, 2, 4, true>();
   if (!st && encode_fn() == nullptr) st = VITB200_E_NO_TMA;
   return st;
 }
@@ -945,18 +1006,21 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
   int v = g_forced_variant;
   if (v == 0 || (kVariants[v].f16 != 0) != f16) v = pick_variant(p.M, p.N, f16);
   switch (v) {
-    case 1: return launch_variant<false, 128, 32, 2, 4, false>(p, err, s);
-    case 2: return launch_variant<false, 128, 16, 5, 8, false>(p, err, s);
-    case 3: return launch_variant<false, 64, 32, 3, 4, false>(p, err, s);
-    case 4: return launch_variant<false, 128, 32, 2, 2, false>(p, err, s);
-    case 5: return launch_variant<false, 256, 16, 3, 8, false>(p, err, s);
-    case 6: return launch_variant<false, 256, 32, 2, 4, true>(p, err, s);
-    case 7: return launch_variant<false, 256, 16, 5, 8, true>(p, err, s);
-    case 8: return launch_variant<false, 256, 16, 5, 16, true>(p, err, s);
-    case 9: return launch_variant<true, 256, 64, 2, 2, true>(p, err, s);
-    case 10: return launch_variant<true, 128, 64, 2, 2, false>(p, err, s);
-    case 11: return launch_variant<true, 64, 64, 3, 2, false>(p, err, s);
-    case 12: return launch_variant<true, 256, 32, 4, 4, true>(p, err, s);
+    case 1: return launch_variant<kKindTF32, 128, 32, 2, 4, false>(p, err, s);
+    case 2: return launch_variant<kKindTF32, 128, 16, 5, 8, false>(p, err, s);
+    case 3: return launch_variant<kKindTF32, 64, 32, 3, 4, false>(p, err, s);
+    case 4: return launch_variant<kKindTF32, 128, 32, 2, 2, false>(p, err, s);
+    case 5: return launch_variant<kKindTF32, 256, 16, 3, 8, false>(p, err, s);
+    case 6: return launch_variant<kKindTF32, 256, 32, 2, 4, true>(p, err, s);
+    case 7: return launch_variant<kKindTF32, 256, 16, 5, 8, true>(p, err, s);
+    case 8: return launch_variant<kKindTF32, 256, 16, 5, 16, true>(p, err, s);
+    case 9: return launch_variant<kKindF16, 256, 64, 2, 2, true>(p, err, s);
+    case 10: return launch_variant<kKindF16, 128, 64, 2, 2, false>(p, err, s);
+    case 11: return launch_variant<kKindF16, 64, 64, 3, 2, false>(p, err, s);
+    case 12: return launch_variant<kKindF16, 256, 32, 4, 4, true>(p, err, s);
+    case 13: return launch_variant<kKindF16SD, 256, 64, 2, 1, true>(p, err, s);
+    case 14: return launch_variant<kKindF16SD, 128, 64, 2, 1, false>(p, err, s);
+    case 15: return launch_variant<kKindF16, 256, 64, 2, 4, true>(p, err, s);
     default: return VITB200_E_UNSUPPORTED;
   }
 }
