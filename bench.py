@@ -78,8 +78,8 @@ def parse_args():
     ap.add_argument("--mode", choices=["full", "roofline"], default="full",
                     help="roofline: time only the dominant GEMM launch (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None, help="override images per GPU")
-    ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS), default="fc1",
-                    help="roofline mode: which block GEMM to time")
+    ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS) + ["attention"], default="fc1",
+                    help="roofline mode: which block GEMM (or the attention) to time")
     return ap.parse_args()
 
 
@@ -438,6 +438,34 @@ def p50_bs1(state, img, dev, iters: int = 200) -> dict:
     return {"graph_ms": graph, "eager_ms": eager}
 
 
+def attention_roofline(dev, B: int, T: int, reps: int = 10):
+    """Times the FP16-split attention (vitb200_attention_f16: splits of q, k,
+    V^T, then the attention kernel) on [B, T, 768] inputs; returns ms per call."""
+    from vit_cuda import _lib
+    lib = _lib.lib
+    s = torch.cuda.current_stream().cuda_stream
+    q, k, v = (torch.randn(B, T, 768, device=dev) for _ in range(3))
+    o = torch.empty_like(q)
+    ws = torch.empty(lib.vitb200_attention_f16_workspace_bytes(B, T, 12), dtype=torch.uint8,
+                     device=dev)
+
+    def launch():
+        _lib.check(lib.vitb200_attention_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                             o.data_ptr(), B, T, 12, 768, 768, 768, 768, 0.125,
+                                             1.0, 1.0, ws.data_ptr(), ws.numel(), s), "attention")
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
 def run_roofline_only(args):
     """The dominant kernel alone (fc1 shape for `batch` images), a small case
     for profilers; prints one JSON line with its CUDA-event time."""
@@ -447,7 +475,14 @@ def run_roofline_only(args):
     batch, img = CONFIGS[args.config]
     if args.batch:
         batch = args.batch
-    M = batch * ((img // 16) ** 2 + 1)
+    T = (img // 16) ** 2 + 1
+    M = batch * T
+    if args.kernel == "attention":
+        ms = attention_roofline(dev, batch, T, reps=max(1, args.steps))
+        emit({"mode": "roofline", "kernel": "attention f16 (splits + attention_f16_kernel)",
+              "B": batch, "T": T, "heads": 12, "call_ms": ms,
+              "algorithmic_tflops": 4.0 * batch * 12 * T * T * 64 / (ms * 1e-3) / 1e12})
+        return
     N, K = ROOFLINE_GEMMS[args.kernel][:2]
     ms = gemm_roofline(dev, M, args.kernel, reps=max(1, args.steps))
     emit({"mode": "roofline", "kernel": f"gemm f16x3 {args.kernel}", "M": M, "N": N, "K": K,
