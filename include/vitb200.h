@@ -201,8 +201,8 @@ int vitb200_attention(const float* q, const float* k, const float* v, float* o,
 /* The same attention with FP16-split operands (three FP16 tensor-core
  * products per multiply, FP32 accuracy; the form the model's block path
  * uses). k and v are multiplied by k_scale and v_scale (powers of two, undone
- * exactly) before the split; the caller chooses them so that |k * k_scale| and
- * |v * v_scale| stay below 16 and |q| below 32768 (larger values set the
+ * exactly; 1 is fine) before the split; |q|, |k * k_scale| and |v * v_scale|
+ * must stay below 32768 (larger values set the
  * device error). The workspace holds the FP16 splits of q, k and V^T. No
  * reference counterpart beyond flash_attn_2_forward_cuda's semantics. */
 size_t vitb200_attention_f16_workspace_bytes(int B, int T, int heads);
@@ -265,7 +265,7 @@ typedef struct vitb200_block_params {
     /* attn_f16 != 0: the attention runs on FP16 splits (as
      * vitb200_attention_f16), its q, k, v written by the QKV GEMM multiplied by
      * q_scale, k_scale, v_scale (powers of two). The caller guarantees
-     * |q * q_scale| < 32768 and |k * k_scale|, |v * v_scale| < 16 (bounds as
+     * |q * q_scale|, |k * k_scale| and |v * v_scale| < 32768 (bounds as
      * above). 0: TF32 pairs. */
     int attn_f16;
     float q_scale, k_scale, v_scale;

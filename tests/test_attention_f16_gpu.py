@@ -16,6 +16,7 @@ pytestmark = pytest.mark.gpu
 
 
 def pow2_scale(x, limit=8.0):
+    """A power-of-two scale as the model would pass (any power of two is exact)."""
     m = float(x.abs().max())
     return 2.0 ** math.floor(math.log2(limit / m)) if m > 0 else 1.0
 
@@ -83,7 +84,8 @@ def test_attention_f16_matches_tf32_path(vlib, cuda):
 
 
 def test_attention_f16_range_error(vlib, cuda):
-    """A k scale that leaves |k * k_scale| >= 16 is reported (device error)."""
+    """A k scale that takes |k * k_scale| past the split's range is reported
+    (device error)."""
     q, k, v = (torch.randn(1, 8, 768, device=cuda) for _ in range(3))
-    run_attn_f16(vlib, q, k, v, 0.125, k_scale=64.0, v_scale=1.0)
+    run_attn_f16(vlib, q, k, v, 0.125, k_scale=2.0 ** 16, v_scale=1.0)
     assert vlib.device_error(clear=True) == 6

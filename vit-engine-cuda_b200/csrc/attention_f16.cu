@@ -11,20 +11,21 @@
 //
 // Operands, written by the QKV GEMM epilogue (kModeQKVAttn16):
 //   q16  [2][M][E]              hi, lo*2^11 of q * q_scale
-//   k16  [3][M][E]              hi, lo*2^11, hi*2^11 of k * k_scale
-//   vt16 [3][B*heads][64][T8]   the same three planes of (v * v_scale)^T per
+//   k16  [2][M][E]              the same two planes of k * k_scale
+//   vt16 [2][B*heads][64][T8]   the same two planes of (v * v_scale)^T per
 //                               (image, head), T8 = T rounded up to 8
-// Each of the three products carries 2^11 (hi*(hi*2^11), hi*(lo*2^11),
-// (lo*2^11)*hi), so one accumulator holds all of them: S accumulates
-// 2^11 q_scale k_scale (q.k), O accumulates 2^11 v_scale (p.v), and the
-// softmax / output undo those powers of two exactly.
+// Per 64-wide tile the two cross products (hi*(lo*2^11), (lo*2^11)*hi) are
+// accumulated first, then the first hi*hi product folds them in with
+// tcgen05.mma's scale-input-d (D = A*B + D*2^-11) and the rest of hi*hi
+// follows: S holds q_scale k_scale (q.k) and O_j v_scale (p.v); the softmax
+// and the output undo those powers of two exactly.
 //
 // Blackwell mapping: persistent CTAs (one per SM) walk work items = (image,
 // head, pair of 128-row query tiles), 384 threads:
-//  * warp 0 (TMA): an item's Q tiles into one of two Q buffers (the next item's
-//    Q lands while the current item runs), then per 64-key tile the K tile and
-//    the V^T tile into a two-stage ring; keys past T arrive as zeros (the V^T
-//    map's key extent is T);
+//  * warp 0 (TMA): an item's Q tiles (loaded once the previous item's last S
+//    is issued), then per 64-key tile the K tile and the V^T tile into a
+//    four-stage ring; keys past T arrive as zeros (the V^T map's key extent
+//    is T);
 //  * warp 1 (MMA, one thread): S_g = Q_g K^T for each query tile g into TMEM,
 //    then O_g = P_g V with P_g read from TMEM as the A operand;
 //  * warpgroups 1 and 2 (softmax of query tile 0 and 1, one row per thread):
@@ -52,11 +53,12 @@ constexpr int kQT = 2;                           // query tiles per work item
 constexpr int kThreadsF = 384;
 constexpr int kQTileBytes = 2 * kQ * kD * 2;     // hi + lo planes: 32 KB
 constexpr int kQBufBytes = kQT * kQTileBytes;    // 64 KB
-constexpr int kKTileBytes = 3 * kKV * kD * 2;    // 24 KB
-constexpr int kVTileBytes = 3 * kD * kKV * 2;    // 24 KB
+constexpr int kKTileBytes = 2 * kKV * kD * 2;    // 16 KB
+constexpr int kVTileBytes = 2 * kD * kKV * 2;    // 16 KB
 constexpr int kStageBytesF = kKTileBytes + kVTileBytes;
-constexpr int kStagesF = 2;
-constexpr int kSmemF = 2 * kQBufBytes + kStagesF * kStageBytesF + 1024;
+constexpr int kStagesF = 4;  // K/V ring depth
+constexpr int kQBufs = 1;    // Q buffers (the next item's Q loads once the last S is issued)
+constexpr int kSmemF = kQBufs * kQBufBytes + kStagesF * kStageBytesF + 1024;
 constexpr int kPlaneQ = kQ * 128;                // bytes between Q planes (128-byte rows)
 constexpr int kPlaneKV = kKV * 128;              // bytes between K / V^T planes
 // TMEM: per query tile two sets of [S (64 cols; P's FP16 split overwrites it:
@@ -82,8 +84,8 @@ struct AttnF16Args {
   int nq;         // query tiles per image
   int qpairs;     // ceil(nq / 2)
   int n_items;    // images * heads * qpairs
-  float s_scale;  // softmax scale / (2^11 * q_scale * k_scale)
-  float o_scale;  // 1 / (2^11 * v_scale)
+  float s_scale;  // log2(e) * softmax scale / (q_scale * k_scale): S -> log2 units
+  float o_scale;  // 1 / v_scale
   float* o;       // fp32 O [M][ldo] or null
   int64_t ldo;
   float* o_pair;  // TF32 pair of O (planes hi | lo) or null
@@ -139,8 +141,8 @@ __global__ void __launch_bounds__(kThreadsF, 1)
                          const __grid_constant__ CUtensorMap tmap_k,
                          const __grid_constant__ CUtensorMap tmap_vt, const AttnF16Args a) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full[2];
-  __shared__ __align__(8) uint64_t q_empty[2];
+  __shared__ __align__(8) uint64_t q_full[kQBufs];
+  __shared__ __align__(8) uint64_t q_empty[kQBufs];
   __shared__ __align__(8) uint64_t kv_full[kStagesF];
   __shared__ __align__(8) uint64_t kv_empty[kStagesF];
   __shared__ __align__(8) uint64_t s_full[kQT][2];
@@ -154,11 +156,11 @@ __global__ void __launch_bounds__(kThreadsF, 1)
   int* err = a.err;
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sq0 = base;                            // two Q buffers
-  uint8_t* skv0 = base + 2 * kQBufBytes;          // K/V ring
+  uint8_t* sq0 = base;                            // Q buffers
+  uint8_t* skv0 = base + kQBufs * kQBufBytes;     // K/V ring
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kQBufs; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
     }
@@ -199,8 +201,10 @@ __global__ void __launch_bounds__(kThreadsF, 1)
       bool ok = true;
       for (int item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++local) {
         const Item it = decode_item(a, item);
-        const int qb = local & 1;
-        if (!mbar_wait(&q_empty[qb], ((local >> 1) & 1) ^ 1u, err, kErrWaitEmpty)) break;
+        const int qb = local % kQBufs;
+        if (!mbar_wait(&q_empty[qb], static_cast<uint32_t>((local / kQBufs) & 1) ^ 1u, err,
+                       kErrWaitEmpty))
+          break;
         uint8_t* sq = sq0 + qb * kQBufBytes;
         const int row0 = it.b * a.T;
         ++q_issued;
@@ -225,9 +229,9 @@ __global__ void __launch_bounds__(kThreadsF, 1)
         }
       }
       // Every copy issued must land before the CTA can exit.
-      for (int qb = 0; qb < 2; ++qb)
+      for (int qb = 0; qb < kQBufs; ++qb)
         if (q_issued > qb) {
-          const int fills = (q_issued - qb + 1) / 2;
+          const int fills = (q_issued - qb + kQBufs - 1) / kQBufs;
           f16_drain_wait(&q_full[qb], static_cast<uint32_t>((fills - 1) & 1), err);
         }
       for (int s = 0; s < kStagesF; ++s)
@@ -245,8 +249,10 @@ __global__ void __launch_bounds__(kThreadsF, 1)
       bool ok = true;
       for (int item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++local) {
         const Item it = decode_item(a, item);
-        const int qb = local & 1;
-        if (!mbar_wait(&q_full[qb], (local >> 1) & 1, err, kErrWaitFull)) break;
+        const int qb = local % kQBufs;
+        if (!mbar_wait(&q_full[qb], static_cast<uint32_t>((local / kQBufs) & 1), err,
+                       kErrWaitFull))
+          break;
         tc_fence_after();
         const uint32_t q_addr = smem_addr(sq0 + qb * kQBufBytes);
         auto issue_s = [&](int j) -> bool {
@@ -268,17 +274,23 @@ __global__ void __launch_bounds__(kThreadsF, 1)
             tc_fence_after();
             const uint32_t d = tmem_base + static_cast<uint32_t>(g * kTileColsF + set * kSetColsF);
             const uint32_t qa = q_addr + g * kQTileBytes;
+            // Descriptors of slice 0; a 16-wide K slice further is +32 bytes,
+            // i.e. +2 in the descriptor's address field.
+            const uint64_t qh = make_sdesc_kmajor(qa, 128);
+            const uint64_t ql = make_sdesc_kmajor(qa + kPlaneQ, 128);
+            const uint64_t kh = make_sdesc_kmajor(k_addr, 128);
+            const uint64_t kl = make_sdesc_kmajor(k_addr + kPlaneKV, 128);
 #pragma unroll
             for (int kk = 0; kk < kD / 16; ++kk) {
-              const uint32_t off = static_cast<uint32_t>(kk * 32);
-              const uint64_t qh = make_sdesc_kmajor(qa + off, 128);
-              const uint64_t ql = make_sdesc_kmajor(qa + kPlaneQ + off, 128);
-              const uint64_t kh = make_sdesc_kmajor(k_addr + off, 128);
-              const uint64_t kl = make_sdesc_kmajor(k_addr + kPlaneKV + off, 128);
-              const uint64_t khh = make_sdesc_kmajor(k_addr + 2 * kPlaneKV + off, 128);
-              umma_f16(d, ql, kh, kIdescSF, kk ? 1u : 0u);  // lo * hi
-              umma_f16(d, qh, kl, kIdescSF, 1u);            // hi * lo
-              umma_f16(d, qh, khh, kIdescSF, 1u);           // hi * hi
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
+              umma_f16(d, ql + o, kh + o, kIdescSF, kk ? 1u : 0u);  // lo * hi
+              umma_f16(d, qh + o, kl + o, kIdescSF, 1u);            // hi * lo
+            }
+            umma_f16_sd11(d, qh, kh, kIdescSF);  // hi * hi + cross * 2^-11
+#pragma unroll
+            for (int kk = 1; kk < kD / 16; ++kk) {
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
+              umma_f16(d, qh + o, kh + o, kIdescSF, 1u);            // hi * hi
             }
             umma_commit(&s_full[g][set]);
           }
@@ -299,16 +311,20 @@ __global__ void __launch_bounds__(kThreadsF, 1)
                 tmem_base + static_cast<uint32_t>(g * kTileColsF + set * kSetColsF);
             const uint32_t p_lo = p_hi + 32;
             const uint32_t d = p_hi + 64;
+            const uint64_t vh = make_sdesc_kmajor(v_addr, 128);
+            const uint64_t vl = make_sdesc_kmajor(v_addr + kPlaneKV, 128);
 #pragma unroll
             for (int kk = 0; kk < kKV / 16; ++kk) {
-              const uint32_t off = static_cast<uint32_t>(kk * 32);
-              const uint64_t vh = make_sdesc_kmajor(v_addr + off, 128);
-              const uint64_t vl = make_sdesc_kmajor(v_addr + kPlaneKV + off, 128);
-              const uint64_t vhh = make_sdesc_kmajor(v_addr + 2 * kPlaneKV + off, 128);
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
               const uint32_t col = static_cast<uint32_t>(kk * 8);
-              umma_f16_tmem_a(d, p_lo + col, vh, kIdescPVF, kk ? 1u : 0u);  // lo * hi
-              umma_f16_tmem_a(d, p_hi + col, vl, kIdescPVF, 1u);            // hi * lo
-              umma_f16_tmem_a(d, p_hi + col, vhh, kIdescPVF, 1u);           // hi * hi
+              umma_f16_tmem_a(d, p_lo + col, vh + o, kIdescPVF, kk ? 1u : 0u);  // lo * hi
+              umma_f16_tmem_a(d, p_hi + col, vl + o, kIdescPVF, 1u);            // hi * lo
+            }
+            umma_f16_tmem_a_sd11(d, p_hi, vh, kIdescPVF);  // hi * hi + cross * 2^-11
+#pragma unroll
+            for (int kk = 1; kk < kKV / 16; ++kk) {
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
+              umma_f16_tmem_a(d, p_hi + kk * 8, vh + o, kIdescPVF, 1u);        // hi * hi
             }
             umma_commit(&pv_full[g][set]);
           }
@@ -387,19 +403,22 @@ __global__ void __launch_bounds__(kThreadsF, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) s[half * 32 + c] = tt[c];
         }
+        // Online softmax in base 2: exp(x * scale - m) = 2^(x * s_scale - m'),
+        // with s_scale = scale * log2(e) (and the operand scales) and m' the
+        // running maximum in the same units; one FMA rounds each argument.
         const int nvalid = min(kKV, a.T - j * kKV);
         float cmax = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kKV; ++c) {
-          s[c] = (c < nvalid) ? s[c] * a.s_scale : -INFINITY;
+          s[c] = (c < nvalid) ? s[c] : -INFINITY;
           cmax = fmaxf(cmax, s[c]);
         }
-        const float m_new = fmaxf(m_run, cmax);
-        const float alpha = expf(m_run - m_new);
+        const float m_new = fmaxf(m_run, cmax * a.s_scale);
+        const float alpha = exp2f(m_run - m_new);
         float psum = 0.f;
 #pragma unroll
         for (int c = 0; c < kKV; ++c) {
-          s[c] = expf(s[c] - m_new);
+          s[c] = exp2f(fmaf(s[c], a.s_scale, -m_new));
           psum += s[c];
         }
         l_run = l_run * alpha + psum;
@@ -407,11 +426,10 @@ __global__ void __launch_bounds__(kThreadsF, 1)
         float ph[32], pl[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          __half h0, l0, h1, l1;
-          h16_split(s[2 * c], h0, l0);
-          h16_split(s[2 * c + 1], h1, l1);
-          ph[c] = __uint_as_float(pack_h2(h0, h1));
-          pl[c] = __uint_as_float(pack_h2(l0, l1));
+          uint32_t hw, lw;
+          h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
+          ph[c] = __uint_as_float(hw);
+          pl[c] = __uint_as_float(lw);
         }
         __syncwarp();
         tmem_st_32x32b_x32(scol, ph);
@@ -459,13 +477,8 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           for (int c = 0; c < kD; c += 8) {
             uint32_t hw[4], lw[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              __half h0, l0, h1, l1;
-              h16_split(o[c + 2 * u] * inv, h0, l0);
-              h16_split(o[c + 2 * u + 1] * inv, h1, l1);
-              hw[u] = pack_h2(h0, h1);
-              lw[u] = pack_h2(l0, l1);
-            }
+            for (int u = 0; u < 4; ++u)
+              h16_split2(o[c + 2 * u] * inv, o[c + 2 * u + 1] * inv, hw[u], lw[u]);
             *reinterpret_cast<uint4*>(hp + c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             *reinterpret_cast<uint4*>(hp + a.hplane + c) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
@@ -508,14 +521,14 @@ int attention_f16_launch(const uint16_t* q16, const uint16_t* k16, int64_t ld, c
     return VITB200_E_ALIGNMENT;
   CUtensorMap tq, tk, tvt;
   if (int st = make_planes_map(&tq, q16, M, static_cast<int>(ld), 2, kQ, kD, 1)) return st;
-  if (int st = make_planes_map(&tk, k16, M, static_cast<int>(ld), 3, kKV, kD, 1)) return st;
+  if (int st = make_planes_map(&tk, k16, M, static_cast<int>(ld), 2, kKV, kD, 1)) return st;
   {
-    // V^T [3][B*heads][64][T8]: keys innermost with extent T (zero fill past T).
+    // V^T [2][B*heads][64][T8]: keys innermost with extent T (zero fill past T).
     const uint64_t bh = static_cast<uint64_t>(B) * heads;
     const uint64_t t8 = static_cast<uint64_t>(T8);
-    const uint64_t dims[4] = {static_cast<uint64_t>(T), kD, bh, 3};
+    const uint64_t dims[4] = {static_cast<uint64_t>(T), kD, bh, 2};
     const uint64_t strides[3] = {t8 * 2, kD * t8 * 2, bh * kD * t8 * 2};
-    const uint32_t box[4] = {kKV, kD, 1, 3};
+    const uint32_t box[4] = {kKV, kD, 1, 2};
     if (int st = encode_tmap_typed(&tvt, 4, vt16, dims, strides, box, 1, 1)) return st;
   }
   AttnF16Args a;
@@ -527,8 +540,8 @@ int attention_f16_launch(const uint16_t* q16, const uint16_t* k16, int64_t ld, c
   const int64_t items = static_cast<int64_t>(B) * heads * a.qpairs;
   if (items > 0x7fffffffLL) return VITB200_E_UNSUPPORTED;
   a.n_items = static_cast<int>(items);
-  a.s_scale = scale / (kH16LoScale * q_scale * k_scale);
-  a.o_scale = 1.f / (kH16LoScale * v_scale);
+  a.s_scale = 1.4426950408889634f * scale / (q_scale * k_scale);
+  a.o_scale = 1.f / v_scale;
   a.o = o;
   a.ldo = ldo;
   a.o_pair = o_pair;

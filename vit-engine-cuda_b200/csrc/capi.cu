@@ -471,7 +471,7 @@ int vitb200_attention(const float* q, const float* k, const float* v, float* o, 
 
 static size_t vt16_halves(int B, int T, int heads) {
   const size_t T8 = (static_cast<size_t>(T) + 7) / 8 * 8;
-  return 3 * static_cast<size_t>(B) * heads * 64 * T8;
+  return 2 * static_cast<size_t>(B) * heads * 64 * T8;
 }
 
 size_t vitb200_attention_f16_workspace_bytes(int B, int T, int heads) {
@@ -479,7 +479,7 @@ size_t vitb200_attention_f16_workspace_bytes(int B, int T, int heads) {
   Carve c{nullptr, 0};
   const size_t n = static_cast<size_t>(B) * T * heads * 64;
   c.take((2 * n + 1) / 2);         // q16: 2 planes of halves
-  c.take((3 * n + 1) / 2);         // k16: 3 planes
+  c.take((2 * n + 1) / 2);         // k16: 2 planes
   c.take((vt16_halves(B, T, heads) + 1) / 2);
   return align_up(c.off, 256);
 }
@@ -498,14 +498,14 @@ int vitb200_attention_f16(const float* q, const float* k, const float* v, float*
   const size_t n = static_cast<size_t>(M) * width;
   Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
   uint16_t* q16 = reinterpret_cast<uint16_t*>(c.take((2 * n + 1) / 2));
-  uint16_t* k16 = reinterpret_cast<uint16_t*>(c.take((3 * n + 1) / 2));
+  uint16_t* k16 = reinterpret_cast<uint16_t*>(c.take((2 * n + 1) / 2));
   uint16_t* vt16 = reinterpret_cast<uint16_t*>(c.take((vt16_halves(B, T, heads) + 1) / 2));
   if (!workspace || !c.fits()) return VITB200_E_WORKSPACE;
   if (int st = check_ready()) return st;
   cudaStream_t s = as_stream(stream);
   if (int st = split_f16_launch(q, M, static_cast<int>(width), ldq, 1.f, q16, width, 2, s))
     return st;
-  if (int st = split_f16_launch(k, M, static_cast<int>(width), ldk, k_scale, k16, width, 3, s))
+  if (int st = split_f16_launch(k, M, static_cast<int>(width), ldk, k_scale, k16, width, 2, s))
     return st;
   if (int st = split_transpose_v_f16_launch(v, ldv, B, T, heads, v_scale, vt16, s)) return st;
   return attention_f16_launch(q16, k16, width, vt16, (T + 7) / 8 * 8, o, ldo, nullptr, 0, 0,
@@ -662,7 +662,7 @@ size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve
   b->x = c->take(static_cast<size_t>(d.M) * D);
   b->pair_a = c->take(2 * std::max(static_cast<size_t>(d.M) * D,
                                    static_cast<size_t>(d.Mp) * d.Kpatch));
-  // qk / vt also hold the FP16 attention's q16 + k16 (5 planes of halves) and vt16.
+  // qk / vt also hold the FP16 attention's q16 + k16 (4 planes of halves) and vt16.
   b->qk = c->take(2 * static_cast<size_t>(d.M) * 2 * D);
   b->vt = c->take(std::max(vt_pair_floats(batch, d.T, p->num_heads),
                            (vt16_halves(batch, d.T, p->num_heads) + 1) / 2));
@@ -744,7 +744,7 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
       g.epi.q16 = q16;
       g.epi.k16 = k16;
       g.epi.vt16 = vt16;
-      g.epi.vt16_plane = static_cast<int64_t>(vt16_halves(batch, d.T, p->num_heads) / 3);
+      g.epi.vt16_plane = static_cast<int64_t>(vt16_halves(batch, d.T, p->num_heads) / 2);
       g.epi.T4 = T8;
       g.epi.q_scale = w.q_scale;
       g.epi.k_scale = w.k_scale;

@@ -353,6 +353,17 @@ __device__ __forceinline__ void umma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem
       : "memory");
 }
 
+// D[tmem] = A[tmem] * B[smem desc] + D * 2^-11 (scale-input-d), kind::f16, one CTA.
+__device__ __forceinline__ void umma_f16_tmem_a_sd11(uint32_t d_tmem, uint32_t a_tmem,
+                                                     uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p, 11;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns from registers: thread i writes lane (base+i).
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(

@@ -400,9 +400,9 @@ int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int head
   return cuda_status(cudaGetLastError());
 }
 
-// v[B*T][ldv] * scale -> vt16[3][B*heads][64][T8]: per (image, head) the
-// transposed FP16 split planes hi, lo*2^11, hi*2^11 (the FP16 attention's V^T
-// operand). Same 32x32 shared-memory transpose as the TF32 version.
+// v[B*T][ldv] * scale -> vt16[2][B*heads][64][T8]: per (image, head) the
+// transposed FP16 split planes hi, lo*2^11 (the FP16 attention's V^T operand).
+// Same 32x32 shared-memory transpose as the TF32 version.
 __global__ void split_transpose_v_f16_kernel(const float* __restrict__ v, int64_t ldv, int T,
                                              int heads, int T8, float scale,
                                              uint16_t* __restrict__ vt, int64_t plane, int* err) {
@@ -421,13 +421,12 @@ __global__ void split_transpose_v_f16_kernel(const float* __restrict__ v, int64_
     const int t = t0 + tx;
     if (t < T) {
       const float x = __fmul_rn(tile[tx][k], scale);
-      bad |= !(fabsf(x) < 16.f);
+      bad |= !(fabsf(x) < kH16Limit);
       __half hi, lo;
       h16_split(x, hi, lo);
       const int64_t idx = (static_cast<int64_t>(bh) * 64 + d0 + k) * T8 + t;
       vt[idx] = __half_as_ushort(hi);
       vt[idx + plane] = __half_as_ushort(lo);
-      vt[idx + 2 * plane] = __half_as_ushort(__float2half_rn(__half2float(hi) * kH16LoScale));
     }
   }
   if (bad) report_error(err, kErrF16Range);

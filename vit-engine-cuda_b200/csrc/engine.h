@@ -16,8 +16,8 @@ enum EpiMode : int {
   kModeQKVAttn = 3, // q|k columns -> TF32 pair rows [2][M][2E]; v columns -> the
                     // per-head transposed pair vt[2][B*heads][64][T4] (attention's V^T)
   kModeQKVAttn16 = 4, // FP16 splits for the FP16 attention: q*q_scale -> q16[2][M][E];
-                      // k*k_scale -> k16[3][M][E]; v*v_scale transposed per (image,
-                      // head) -> vt16[3][B*heads][64][T4] (T4 = T rounded up to 8 here)
+                      // k*k_scale -> k16[2][M][E]; v*v_scale transposed per (image,
+                      // head) -> vt16[2][B*heads][64][T4] (T4 = T rounded up to 8 here)
 };
 
 struct GemmEpilogue {
@@ -123,8 +123,8 @@ int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* 
                      float* o_pair, int64_t pair_ld, int64_t pair_plane, int B, int T, int heads,
                      float scale, cudaStream_t s, uint16_t* o_h16 = nullptr, int64_t h16_ld = 0,
                      int64_t h16_plane = 0);
-// FP16-split attention (attention_f16.cu): q16 [2][B*T][ld], k16 [3][B*T][ld]
-// (head h at columns h*64..), vt16 [3][B*heads][64][T8] as the QKV epilogue's
+// FP16-split attention (attention_f16.cu): q16, k16 [2][B*T][ld] (head h at
+// columns h*64..), vt16 [2][B*heads][64][T8] as the QKV epilogue's
 // kModeQKVAttn16 writes them (q, k, v multiplied by q_scale, k_scale, v_scale,
 // powers of two). Writes fp32 O, its TF32 pair and/or its FP16 split.
 int attention_f16_prepare_device();
@@ -133,7 +133,7 @@ int attention_f16_launch(const uint16_t* q16, const uint16_t* k16, int64_t ld, c
                          int64_t pair_plane, uint16_t* o_h16, int64_t h16_ld, int64_t h16_plane,
                          int B, int T, int heads, float scale, float q_scale, float k_scale,
                          float v_scale, cudaStream_t s);
-// v[B*T][ldv] * scale -> vt16 [3][B*heads][64][T8] (hi, lo*2^11, hi*2^11).
+// v[B*T][ldv] * scale -> vt16 [2][B*heads][64][T8] (hi, lo*2^11).
 int split_transpose_v_f16_launch(const float* v, int64_t ldv, int B, int T, int heads, float scale,
                                  uint16_t* vt16, cudaStream_t s);
 // V[B*T][ldv] (head h at columns h*64..) -> vt pair [2][B*heads][64][T4].

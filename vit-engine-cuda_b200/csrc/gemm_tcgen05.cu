@@ -223,7 +223,7 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
     for (int j = 0; j < 32; ++j) v[j] = v[j] * sc;  // exact: a power of two
     if (part < 2) {
       h16_slab_store(v, stg, lane, m_base, a.M, part == 0 ? e.q16 : e.k16, E, a.M * E,
-                     n0 - part * E, part == 1);
+                     n0 - part * E, false);
       return;
     }
     // V: transposed per (image, head); lanes hold consecutive tokens, so each
@@ -241,7 +241,6 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
       const int64_t o = static_cast<int64_t>(j) * e.T4;
       dst[o] = hi;
       dst[o + e.vt16_plane] = lo;
-      dst[o + 2 * e.vt16_plane] = __float2half_rn(__half2float(hi) * kH16LoScale);
     }
     return;
   }
@@ -600,24 +599,25 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_tf32(d_tmem, da, db, Cfg::kIdesc, acc);
             }
           };
+          // Descriptors of the stage's first K slice; one MMA's K further is
+          // +32 bytes, i.e. +2 in the descriptor's address field.
+          const uint64_t dah = make_sdesc_kmajor(a_hi, Cfg::kRowBytes);
+          const uint64_t dal = make_sdesc_kmajor(a_lo, Cfg::kRowBytes);
+          const uint64_t dbh = make_sdesc_kmajor(b_hi, Cfg::kRowBytes);
+          const uint64_t dbl = make_sdesc_kmajor(b_lo, Cfg::kRowBytes);
+          const uint64_t dbhh = make_sdesc_kmajor(b_hh, Cfg::kRowBytes);
           if constexpr (Cfg::SD) {
             // The stage's cross products (each scaled by 2^11) first, then
             // hi * hi with the accumulator scaled by 2^-11 on the first one.
 #pragma unroll
             for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
-              const uint32_t koff = static_cast<uint32_t>(kk * 32);
-              const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
-              const uint64_t dal = make_sdesc_kmajor(a_lo + koff, Cfg::kRowBytes);
-              const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
-              const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, Cfg::kRowBytes);
-              mma(dal, dbh, kk == 0 ? 0u : 1u);  // lo * hi
-              mma(dah, dbl, 1u);                 // hi * lo
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
+              mma(dal + o, dbh + o, kk == 0 ? 0u : 1u);  // lo * hi
+              mma(dah + o, dbl + o, 1u);                 // hi * lo
             }
 #pragma unroll
             for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
-              const uint32_t koff = static_cast<uint32_t>(kk * 32);
-              const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
-              const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
               if (kk == 0) {
                 if constexpr (PAIR) {
                   umma_f16_pair_sd11(d_tmem, dah, dbh, Cfg::kIdesc);
@@ -625,22 +625,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                   umma_f16_sd11(d_tmem, dah, dbh, Cfg::kIdesc);
                 }
               } else {
-                mma(dah, dbh, 1u);  // hi * hi
+                mma(dah + o, dbh + o, 1u);  // hi * hi
               }
             }
           } else {
 #pragma unroll
             for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
-              const uint32_t koff = static_cast<uint32_t>(kk * 32);  // one MMA's K = 32 bytes
-              const uint64_t dah = make_sdesc_kmajor(a_hi + koff, Cfg::kRowBytes);
-              const uint64_t dal = make_sdesc_kmajor(a_lo + koff, Cfg::kRowBytes);
-              const uint64_t dbh = make_sdesc_kmajor(b_hi + koff, Cfg::kRowBytes);
-              const uint64_t dbl = make_sdesc_kmajor(b_lo + koff, Cfg::kRowBytes);
-              const uint64_t dbhh = make_sdesc_kmajor(b_hh + koff, Cfg::kRowBytes);
+              const uint64_t o = static_cast<uint64_t>(2 * kk);
               const uint32_t acc0 = (chunk_first && kk == 0) ? 0u : 1u;
-              mma(dal, dbh, acc0);  // lo * hi
-              mma(dah, dbl, 1u);    // hi * lo
-              mma(dah, dbhh, 1u);   // hi * hi
+              mma(dal + o, dbh + o, acc0);  // lo * hi
+              mma(dah + o, dbl + o, 1u);    // hi * lo
+              mma(dah + o, dbhh + o, 1u);   // hi * hi
             }
           }
           commit(&empty_bar[stage]);  // frees the stage once these MMAs finish

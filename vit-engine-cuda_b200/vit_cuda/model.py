@@ -29,8 +29,7 @@ import torch.nn as nn
 
 from . import _C, _lib
 from ._lib import BlockParams, VitParams, lib
-from .split import (F16_SAFE_BOUND, block_input_bounds, f16_weight, f16_weight_ok,
-                    operand_scale)
+from .split import F16_SAFE_BOUND, block_input_bounds, f16_weight, f16_weight_ok
 
 _BLOCK_KEYS = [
     ("norm1_gamma", "norm1.weight"), ("norm1_beta", "norm1.bias"),
@@ -163,12 +162,10 @@ class ViTCUDA(nn.Module):
                         w[name] = (_split_pair(weight), None, 0.0)
                         kinds[name] = "tf32"
                     keep += [t for t in w[name][:2] if t is not None]
-                # The FP16 attention: |q| within the split's range, k and v
-                # scaled by powers of two into |x| <= 8 (their third plane
-                # hi * 2^11 must stay finite).
-                k_s, v_s = operand_scale(bounds["k"]), operand_scale(bounds["v"])
+                # The FP16 attention: q, k and v within the split's range.
+                k_s = v_s = 1.0
                 attn_f16 = (self.operands == "auto" and bounds["q"] < F16_SAFE_BOUND
-                            and k_s is not None and v_s is not None)
+                            and bounds["k"] < F16_SAFE_BOUND and bounds["v"] < F16_SAFE_BOUND)
                 kinds["attn"] = "f16" if attn_f16 else "tf32"
                 self.gemm_operands.append(kinds)
                 vecs = [blk.norm1_gamma, blk.norm1_beta, blk.qkv_bias, blk.proj_bias,

@@ -96,15 +96,6 @@ def block_input_bounds(blk, embed_dim: int) -> dict[str, float]:
     return {"qkv": ln1, "proj": v, "fc1": ln2, "fc2": max(h, 0.2), "q": q, "k": k, "v": v}
 
 
-def operand_scale(bound: float, target: float = 8.0) -> float | None:
-    """Power of two s with bound * s <= target (None when the bound is not a
-    finite positive number or s would leave [2^-60, 2^60])."""
-    if not (math.isfinite(bound) and bound > 0.0):
-        return None
-    s = 2.0 ** math.floor(math.log2(target / bound))
-    return s if 2.0 ** -60 <= s <= 2.0 ** 60 else None
-
-
 def f16_weight_ok(w: torch.Tensor) -> bool:
     """A weight the FP16 split can carry: finite, and not so small that its
     power-of-two scale leaves the fp32 range."""
