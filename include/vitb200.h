@@ -101,6 +101,21 @@ int vitb200_set_gemm_variant(int variant);
 int vitb200_split_tf32(const float* x, int64_t rows, int cols, int64_t ldx,
                        float* pair, int ldp, void* stream);
 
+/* Image preprocessing, the step before the forward in the reference
+ * (vit_cuda/model.py:180-188: torchvision Resize(resize_short) ->
+ * CenterCrop(crop) -> ToTensor -> Normalize(mean, std)). images: B equal-size
+ * 8-bit RGB images, HWC, image_stride bytes apart (>= H*W*3), on the device.
+ * The shorter side is resized to resize_short (the longer to
+ * floor(resize_short * long / short)) with antialiased bilinear resampling in
+ * fp32, the centred crop x crop window kept (offsets rounded half to even),
+ * and out[B][3][crop][crop] = (x / 255 - mean[c]) / std[c]; mean and std are
+ * 3-element host arrays. VITB200_E_UNSUPPORTED when the resized image is
+ * smaller than the crop (torchvision would pad). */
+int vitb200_preprocess(const uint8_t* images, int B, int H, int W,
+                       int64_t image_stride, int resize_short, int crop,
+                       const float* mean, const float* std, float* out,
+                       void* stream);
+
 /* ---- per-op entry points (reference: csrc/bindings/binding.cpp:5-23) --- */
 
 /* LayerNorm over the last dim E of x[rows][E]: biased variance, affine.

@@ -115,3 +115,21 @@ def test_workspace_too_small_rejected_without_gpu():
 
 def test_qkv_width_not_multiple_of_32_is_unsupported():
     assert lib.vitb200_qkv(1, 1, 1, 1, 4, 40, None, 0, None) == _lib.E_UNSUPPORTED
+
+
+def test_preprocess_argument_checks():
+    """vitb200_preprocess validates before touching the device."""
+    import ctypes
+    from vit_cuda import _lib
+    m = (ctypes.c_float * 3)(0.5, 0.5, 0.5)
+    s = (ctypes.c_float * 3)(0.2, 0.2, 0.2)
+    bad_s = (ctypes.c_float * 3)(0.2, 0.0, 0.2)
+    f = _lib.lib.vitb200_preprocess
+    assert f(None, 0, 10, 10, 300, 256, 224, m, s, None, None) == 0           # empty batch
+    assert f(None, 1, 10, 10, 299, 256, 224, m, s, None, None) == _lib.E_INVALID_ARG  # stride
+    assert f(None, 1, 10, 10, 300, 256, 224, m, s, None, None) == _lib.E_INVALID_ARG  # null
+    assert f(None, -1, 10, 10, 300, 256, 224, m, s, None, None) == _lib.E_INVALID_ARG
+    assert f(None, 1, 10, 10, 300, 256, 224, m, None, None, None) == _lib.E_INVALID_ARG
+    p = ctypes.c_void_p(16)
+    assert f(p, 1, 10, 10, 300, 200, 224, m, s, p, None) == _lib.E_UNSUPPORTED  # crop > resize
+    assert f(p, 1, 10, 10, 300, 256, 224, m, bad_s, p, None) == _lib.E_INVALID_ARG

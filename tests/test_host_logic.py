@@ -62,10 +62,19 @@ def test_ops_reject_cpu_tensors_like_the_reference():
 
 
 def test_package_surface():
+    """vit_cuda.<op> (through the registered torch.ops.vit_cuda ops) and
+    vit_cuda._C.<op> (direct) exist for the eight reference ops and raise the
+    reference wrappers' RuntimeError for non-CUDA inputs alike."""
     for name in ["flash_attn_2", "patch_embed", "pos_encoding", "mlp_forward",
                  "layernorm_forward", "classifier_forward", "qkv_proj", "gemm_bias"]:
         assert callable(getattr(vit_cuda, name))
-        assert getattr(vit_cuda._C, name) is getattr(vit_cuda, name)
+        assert callable(getattr(vit_cuda._C, name))
+    x = torch.randn(1, 4, 768)
+    for mod in (vit_cuda, vit_cuda._C):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            mod.layernorm_forward(x, torch.ones(768), torch.zeros(768), 1e-6)
+        with pytest.raises(RuntimeError, match="CUDA"):
+            mod.qkv_proj(x, torch.randn(2304, 768), torch.randn(2304))
 
 
 def test_model_buffer_names_match_reference():
@@ -127,3 +136,32 @@ def test_linear_bound_and_weight_scale():
     assert not f16_weight_ok(torch.tensor([1e-30]))
     assert not f16_weight_ok(torch.tensor([float("inf")]))
     assert f16_weight_ok(torch.tensor([0.02]))
+
+
+def test_custom_ops_registered_with_fake_shapes():
+    """The ops are registered with torch.library; their fake implementations
+    give the reference ops' output shapes without a GPU."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import vit_cuda  # noqa: F401  (registers torch.ops.vit_cuda.*)
+    ops = torch.ops.vit_cuda
+    with FakeTensorMode():
+        x = torch.empty(2, 197, 768, device="cuda")
+        w = torch.empty(768, 768, device="cuda")
+        b = torch.empty(768, device="cuda")
+        assert ops.flash_attn_2(x, x, x, 0.125).shape == (2, 197, 768)
+        img = torch.empty(2, 3, 224, 224, device="cuda")
+        assert ops.patch_embed(img, w, b).shape == (2, 196, 768)
+        assert ops.pos_encoding(torch.empty(2, 196, 768, device="cuda"),
+                                torch.empty(2, 768, device="cuda"),
+                                torch.empty(197, 768, device="cuda")).shape == (2, 197, 768)
+        o, h = ops.mlp_forward(x, torch.empty(3072, 768, device="cuda"),
+                               torch.empty(3072, device="cuda"),
+                               torch.empty(768, 3072, device="cuda"), b)
+        assert o.shape == (2, 197, 768) and h.shape == (2, 197, 3072)
+        assert ops.layernorm_forward(x, b, b, 1e-6).shape == (2, 197, 768)
+        assert ops.classifier_forward(x, torch.empty(1000, 768, device="cuda"),
+                                      torch.empty(1000, device="cuda")).shape == (2, 1000)
+        assert ops.qkv_proj_packed(x, torch.empty(2304, 768, device="cuda"),
+                                   torch.empty(2304, device="cuda")).shape == (3, 2, 197, 768)
+        assert ops.gemm_bias(x, w, b).shape == (2, 197, 768)
+        assert ops.vit_forward(img, 12345, 1000).shape == (2, 1000)

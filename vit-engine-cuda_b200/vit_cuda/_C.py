@@ -236,6 +236,12 @@ def classifier_forward(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor) -> 
 def qkv_proj(X: torch.Tensor, W: torch.Tensor, B: torch.Tensor) -> list:
     """[q, k, v] = split of X W^T + B at E-column boundaries
     (csrc/ops/qkv_wrapper.cpp:17-55); each output is contiguous [B, N, E]."""
+    qkv = qkv_proj_packed(X, W, B)
+    return [qkv[0], qkv[1], qkv[2]]
+
+
+def qkv_proj_packed(X: torch.Tensor, W: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """qkv_proj's q, k, v as one [3, B, N, N_out/3] tensor (planes contiguous)."""
     _same_device([X, W, B], "qkv_proj")
     Xc, Wc, Bc = _contig(X, "X"), _contig(W, "W"), _contig(B, "B")
     if Xc.dim() != 3:
@@ -256,13 +262,11 @@ def qkv_proj(X: torch.Tensor, W: torch.Tensor, B: torch.Tensor) -> list:
         ws = _workspace(lib.vitb200_qkv_workspace_bytes(M, E), Xc.device)
         _lib.check(lib.vitb200_qkv(Xc.data_ptr(), Wc.data_ptr(), Bc.data_ptr(), qkv.data_ptr(),
                                    M, E, ws.data_ptr(), ws.numel(), _stream()), "qkv_proj")
-        return [qkv[0], qkv[1], qkv[2]]
-    # General N_out: one GEMM into [M, N_out], then contiguous column slices,
-    # exactly as the reference wrapper does.
+        return qkv
+    # General N_out: one GEMM into [M, N_out], then the column thirds made
+    # contiguous, as the reference wrapper does.
     Y = gemm_bias(Xc.reshape(M, E), Wc, Bc)
-    Yr = Y.view(Bb, N, 3, Es)
-    return [Yr.select(2, 0).contiguous(), Yr.select(2, 1).contiguous(),
-            Yr.select(2, 2).contiguous()]
+    return Y.view(Bb, N, 3, Es).permute(2, 0, 1, 3).contiguous()
 
 
 def gemm_bias(X: torch.Tensor, W: torch.Tensor, B: torch.Tensor) -> torch.Tensor:

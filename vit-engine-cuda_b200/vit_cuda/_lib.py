@@ -71,6 +71,8 @@ _SIGNATURES = {
     "vitb200_split_f16": (c_int, [_P, c_int64, c_int, c_int64, c_float, _P, c_int64, c_int, _P]),
     "vitb200_gemm_f16": (c_int, [_P, _P, c_float, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int,
                                  c_int, _P]),
+    "vitb200_preprocess": (c_int, [_P, c_int, c_int, c_int, c_int64, c_int, c_int,
+                                   POINTER(c_float), POINTER(c_float), _P, _P]),
     "vitb200_layernorm": (c_int, [_P, _P, _P, _P, c_int64, c_int, c_float, _P]),
     "vitb200_gemm_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "vitb200_gemm": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int, c_int, c_int, _P, c_size_t, _P]),

@@ -15,8 +15,9 @@ products, FP32 accuracy at twice the TF32 rate) wherever the weights bound
 their input below the split's range, and on TF32 pairs (TF32x3) otherwise;
 ``operands="tf32"`` keeps every GEMM on TF32 pairs.
 
-``ViTBlockCUDA.forward`` keeps the reference's op-by-op block (the ``_C`` ops)
-for callers that drive blocks themselves.
+``ViTBlockCUDA.forward`` keeps the reference's op-by-op block (the registered
+``torch.ops.vit_cuda`` ops) for callers that drive blocks themselves. Under
+``torch.compile`` the fused forward is the registered ``vit_cuda::vit_forward``.
 """
 from __future__ import annotations
 
@@ -27,7 +28,7 @@ from typing import Optional
 import torch
 import torch.nn as nn
 
-from . import _C, _lib
+from . import _lib, library
 from ._lib import BlockParams, VitParams, lib
 from .split import F16_SAFE_BOUND, block_input_bounds, f16_weight, f16_weight_ok
 
@@ -52,14 +53,14 @@ class ViTBlockCUDA(nn.Module):
 
     def forward(self, x, scale, eps):
         residual = x
-        x = _C.layernorm_forward(x, self.norm1_gamma, self.norm1_beta, eps)
-        q, k, v = _C.qkv_proj(x, self.qkv_weight, self.qkv_bias)
-        attn_out = _C.flash_attn_2(q, k, v, scale)
-        attn_out = _C.gemm_bias(attn_out, self.proj_weight, self.proj_bias)
+        x = library.layernorm_forward(x, self.norm1_gamma, self.norm1_beta, eps)
+        q, k, v = library.qkv_proj(x, self.qkv_weight, self.qkv_bias)
+        attn_out = library.flash_attn_2(q, k, v, scale)
+        attn_out = library.gemm_bias(attn_out, self.proj_weight, self.proj_bias)
         x = residual + attn_out
         residual = x
-        x = _C.layernorm_forward(x, self.norm2_gamma, self.norm2_beta, eps)
-        mlp_out = _C.mlp_forward(x, self.fc1_weight, self.fc1_bias, self.fc2_weight,
+        x = library.layernorm_forward(x, self.norm2_gamma, self.norm2_beta, eps)
+        mlp_out = library.mlp_forward(x, self.fc1_weight, self.fc1_bias, self.fc2_weight,
                                  self.fc2_bias)[0]
         return residual + mlp_out
 
@@ -119,7 +120,9 @@ class ViTCUDA(nn.Module):
             raise RuntimeError("pos_embed length must be a square number of patches + 1")
         self.img_size = (grid * 16, grid * 16)
         self.in_chans = self.patch_weight.shape[1] if self.patch_weight.dim() == 4 else 3
-        self._prepared = None  # (key, pairs, params, blocks_array)
+        self._prepared = None  # (key, splits, params, blocks_array, keep-alive, split metadata)
+        self._imported = None  # split weights given to import_splits
+        self._op_id = library.register_model(self)  # torch.ops.vit_cuda.vit_forward
         self._graph = None
 
     # ----------------------------------------------------------- weights
@@ -127,12 +130,52 @@ class ViTCUDA(nn.Module):
         ptrs = tuple(b.data_ptr() for b in self.buffers())
         return (self.patch_weight.device, ptrs)
 
+    def _compute_splits(self) -> tuple[dict, dict]:
+        """The split weights on the model's device: tensors named
+        ``patch.pair``, ``head.pair`` and per block ``blocks.{i}.{gemm}.pair``
+        (TF32 pair) or ``blocks.{i}.{gemm}.f16`` (FP16 planes), plus string
+        metadata: ``blocks.{i}.{gemm}`` = "f16" | "tf32", the FP16 GEMMs'
+        ``.acc_scale`` and ``blocks.{i}.attn`` = "f16" | "tf32"."""
+        tensors = {"patch.pair": _split_pair(self.patch_weight),
+                   "head.pair": _split_pair(self.head_weight)}
+        meta = {}
+        for i, blk in enumerate(self.blocks):
+            bounds = block_input_bounds(blk, 768)
+            for name in ("qkv", "proj", "fc1", "fc2"):
+                weight = getattr(blk, f"{name}_weight")
+                key = f"blocks.{i}.{name}"
+                if (self.operands == "auto" and bounds[name] < F16_SAFE_BOUND
+                        and f16_weight_ok(weight)):
+                    tensors[key + ".f16"], acc_scale = f16_weight(weight.contiguous())
+                    meta[key], meta[key + ".acc_scale"] = "f16", repr(acc_scale)
+                else:
+                    tensors[key + ".pair"] = _split_pair(weight)
+                    meta[key] = "tf32"
+            # The FP16 attention: q, k and v within the split's range.
+            attn_f16 = (self.operands == "auto" and bounds["q"] < F16_SAFE_BOUND
+                        and bounds["k"] < F16_SAFE_BOUND and bounds["v"] < F16_SAFE_BOUND)
+            meta[f"blocks.{i}.attn"] = "f16" if attn_f16 else "tf32"
+        return tensors, meta
+
+    def export_splits(self) -> tuple[dict, dict]:
+        """The split weights prepare() made (for vit_cuda.checkpoint.save_splits)."""
+        prepared = self.prepare()
+        return dict(prepared[1]), dict(prepared[5])
+
+    def import_splits(self, tensors: dict, meta: dict) -> None:
+        """Uses previously exported split weights instead of splitting again
+        (vit_cuda.checkpoint.load_splits checks that they match the weights)."""
+        dev = self.patch_weight.device
+        self._imported = ({k: v.to(dev) for k, v in tensors.items()}, dict(meta))
+        self.prepare(force=True)
+
     def prepare(self, force: bool = False):
         """Splits the linear weights on their device (FP16 splits where the
         block's input bounds allow, TF32 pairs otherwise; ``gemm_operands``
-        records the choice per block) and builds the C parameter block. Runs
-        once per device / weight storage; call it again with force=True after
-        modifying weights in place."""
+        records the choice per block), or takes split weights given to
+        ``import_splits``, and builds the C parameter block. Runs once per
+        device / weight storage; call it again with force=True after modifying
+        weights in place."""
         key = self._source_key()
         if not force and self._prepared is not None and self._prepared[0] == key:
             return self._prepared
@@ -143,44 +186,39 @@ class ViTCUDA(nn.Module):
                 raise RuntimeError(f"ViTCUDA: buffer {name} must be float32")
         with torch.cuda.device(self.patch_weight.device):
             _lib.check(lib.vitb200_init(), "vitb200_init")
-            pairs = {"patch": _split_pair(self.patch_weight), "head": _split_pair(self.head_weight)}
+            imported = getattr(self, "_imported", None)
+            if imported is not None and imported[0]["patch.pair"].device == self.patch_weight.device:
+                splits, meta = imported
+            else:
+                splits, meta = self._compute_splits()
             blocks = (BlockParams * len(self.blocks))()
             keep = []
             self.gemm_operands = []
+            ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
             for i, blk in enumerate(self.blocks):
-                bounds = block_input_bounds(blk, 768)
                 w = {}
                 kinds = {}
                 for name in ("qkv", "proj", "fc1", "fc2"):
-                    weight = getattr(blk, f"{name}_weight")
-                    if (self.operands == "auto" and bounds[name] < F16_SAFE_BOUND
-                            and f16_weight_ok(weight)):
-                        planes, acc_scale = f16_weight(weight.contiguous())
-                        w[name] = (None, planes, acc_scale)
-                        kinds[name] = "f16"
+                    key_ = f"blocks.{i}.{name}"
+                    kinds[name] = meta[key_]
+                    if meta[key_] == "f16":
+                        w[name] = (None, splits[key_ + ".f16"], float(meta[key_ + ".acc_scale"]))
                     else:
-                        w[name] = (_split_pair(weight), None, 0.0)
-                        kinds[name] = "tf32"
-                    keep += [t for t in w[name][:2] if t is not None]
-                # The FP16 attention: q, k and v within the split's range.
-                k_s = v_s = 1.0
-                attn_f16 = (self.operands == "auto" and bounds["q"] < F16_SAFE_BOUND
-                            and bounds["k"] < F16_SAFE_BOUND and bounds["v"] < F16_SAFE_BOUND)
-                kinds["attn"] = "f16" if attn_f16 else "tf32"
+                        w[name] = (splits[key_ + ".pair"], None, 0.0)
+                attn_f16 = meta[f"blocks.{i}.attn"] == "f16"
+                kinds["attn"] = meta[f"blocks.{i}.attn"]
                 self.gemm_operands.append(kinds)
                 vecs = [blk.norm1_gamma, blk.norm1_beta, blk.qkv_bias, blk.proj_bias,
                         blk.norm2_gamma, blk.norm2_beta, blk.fc1_bias, blk.fc2_bias]
                 vecs = [v.contiguous() for v in vecs]
                 keep += vecs
-                ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
                 blocks[i] = BlockParams(
                     vecs[0].data_ptr(), vecs[1].data_ptr(), ptr(w["qkv"][0]), vecs[2].data_ptr(),
                     ptr(w["proj"][0]), vecs[3].data_ptr(), vecs[4].data_ptr(), vecs[5].data_ptr(),
                     ptr(w["fc1"][0]), vecs[6].data_ptr(), ptr(w["fc2"][0]), vecs[7].data_ptr(),
                     ptr(w["qkv"][1]), w["qkv"][2], ptr(w["proj"][1]), w["proj"][2],
                     ptr(w["fc1"][1]), w["fc1"][2], ptr(w["fc2"][1]), w["fc2"][2],
-                    1 if attn_f16 else 0, 1.0, k_s if attn_f16 else 1.0,
-                    v_s if attn_f16 else 1.0)
+                    1 if attn_f16 else 0, 1.0, 1.0, 1.0)
             vecs = {n: getattr(self, n).contiguous() for n in
                     ("patch_bias", "cls_token", "pos_embed", "norm_gamma", "norm_beta",
                      "head_bias")}
@@ -190,14 +228,15 @@ class ViTCUDA(nn.Module):
                 mlp_dim=self.blocks[0].fc1_weight.shape[0], patch=16, in_chans=self.in_chans,
                 img_h=self.img_size[0], img_w=self.img_size[1], num_classes=self.num_classes,
                 ln_eps=self.eps, attn_scale=self.scale,
-                patch_w_pair=pairs["patch"].data_ptr(), patch_b=vecs["patch_bias"].data_ptr(),
+                patch_w_pair=splits["patch.pair"].data_ptr(),
+                patch_b=vecs["patch_bias"].data_ptr(),
                 cls_token=vecs["cls_token"].data_ptr(), pos_embed=vecs["pos_embed"].data_ptr(),
                 blocks=ctypes.cast(blocks, ctypes.POINTER(BlockParams)),
                 norm_w=vecs["norm_gamma"].data_ptr(), norm_b=vecs["norm_beta"].data_ptr(),
-                head_w_pair=pairs["head"].data_ptr(), head_b=vecs["head_bias"].data_ptr())
+                head_w_pair=splits["head.pair"].data_ptr(), head_b=vecs["head_bias"].data_ptr())
             if self.head_weight.shape[0] != self.num_classes:
                 raise RuntimeError("head weight rows must equal num_classes")
-        self._prepared = (key, pairs, params, blocks, keep)
+        self._prepared = (key, splits, params, blocks, keep, meta)
         return self._prepared
 
     @property
@@ -222,6 +261,9 @@ class ViTCUDA(nn.Module):
 
     # ----------------------------------------------------------- forward
     def forward(self, x):
+        # Under torch.compile the fused forward is one registered custom op.
+        if torch.compiler.is_compiling():
+            return torch.ops.vit_cuda.vit_forward(x, self._op_id, self.num_classes)
         # CUDA graph replay path (fixed input shape/address), reference model.py:93-99.
         if self._graph is not None:
             self._static_input.copy_(x)
