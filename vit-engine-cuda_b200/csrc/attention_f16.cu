@@ -58,7 +58,10 @@ constexpr int kVTileBytes = 2 * kD * kKV * 2;    // 16 KB
 constexpr int kStageBytesF = kKTileBytes + kVTileBytes;
 constexpr int kStagesF = 4;  // K/V ring depth
 constexpr int kQBufs = 1;    // Q buffers (the next item's Q loads once the last S is issued)
-constexpr int kSmemF = kQBufs * kQBufBytes + kStagesF * kStageBytesF + 1024;
+// Output transpose buffers: per softmax warp 32 rows x 128 B (32 columns of the
+// FP16 split at a time: 64 B hi, 64 B lo), 16-byte chunks XOR-swizzled by row.
+constexpr int kOutStageBytes = 8 * 32 * 128;
+constexpr int kSmemF = kQBufs * kQBufBytes + kStagesF * kStageBytesF + kOutStageBytes + 1024;
 constexpr int kPlaneQ = kQ * 128;                // bytes between Q planes (128-byte rows)
 constexpr int kPlaneKV = kKV * 128;              // bytes between K / V^T planes
 // TMEM: per query tile two sets of [S (64 cols; P's FP16 split overwrites it:
@@ -105,6 +108,15 @@ __device__ __forceinline__ bool f16_warp_wait(uint64_t* bar, uint32_t parity, in
   if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   return ok != 0;
+}
+
+// 2^x for x <= 0 (the hardware approximation, relative error about 2^-22,
+// below the FP16 split's own; results under 2^-126 flush to zero, where a
+// probability no longer matters against a row maximum of 1).
+__device__ __forceinline__ float exp2_nonpos(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void f16_drain_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -158,6 +170,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sq0 = base;                            // Q buffers
   uint8_t* skv0 = base + kQBufs * kQBufBytes;     // K/V ring
+  uint8_t* sout = skv0 + kStagesF * kStageBytesF; // output transpose buffers
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQBufs; ++i) {
@@ -406,19 +419,20 @@ __global__ void __launch_bounds__(kThreadsF, 1)
         // Online softmax in base 2: exp(x * scale - m) = 2^(x * s_scale - m'),
         // with s_scale = scale * log2(e) (and the operand scales) and m' the
         // running maximum in the same units; one FMA rounds each argument.
-        const int nvalid = min(kKV, a.T - j * kKV);
+        const int nvalid = a.T - j * kKV;
+        if (nvalid < kKV) {  // the ragged last tile (uniform across the warpgroup)
+#pragma unroll
+          for (int c = 0; c < kKV; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
+        }
         float cmax = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kKV; ++c) {
-          s[c] = (c < nvalid) ? s[c] : -INFINITY;
-          cmax = fmaxf(cmax, s[c]);
-        }
+        for (int c = 0; c < kKV; ++c) cmax = fmaxf(cmax, s[c]);
         const float m_new = fmaxf(m_run, cmax * a.s_scale);
-        const float alpha = exp2f(m_run - m_new);
+        const float alpha = exp2_nonpos(m_run - m_new);
         float psum = 0.f;
 #pragma unroll
         for (int c = 0; c < kKV; ++c) {
-          s[c] = exp2f(fmaf(s[c], a.s_scale, -m_new));
+          s[c] = exp2_nonpos(fmaf(s[c], a.s_scale, -m_new));
           psum += s[c];
         }
         l_run = l_run * alpha + psum;
@@ -471,17 +485,42 @@ __global__ void __launch_bounds__(kThreadsF, 1)
             *reinterpret_cast<float4*>(pp + a.pplane + c) = lv;
           }
         }
-        if (a.o_h16) {
-          uint16_t* hp = a.o_h16 + row * a.hld + it.h * kD;
+      }
+      if (ok && a.o_h16) {
+        // FP16 split of O through the warp's transpose buffer, 32 columns at a
+        // time, so that each store instruction writes four whole 64-byte row
+        // segments (lanes 0-3 of each eight: hi, lanes 4-7: lo).
+        const float inv = a.o_scale / l_run;  // rows past T are computed, not stored
+        uint32_t* stg = reinterpret_cast<uint32_t*>(sout) + (warp - 4) * 32 * 32;
+        const int first = (it.qt0 + g) * kQ + quarter * 32;  // token of lane 0's row
+        const int valid = a.T - first;
+        const int64_t row0 = static_cast<int64_t>(it.b) * a.T + first;
 #pragma unroll
-          for (int c = 0; c < kD; c += 8) {
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
             uint32_t hw[4], lw[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              h16_split2(o[c + 2 * u] * inv, o[c + 2 * u + 1] * inv, hw[u], lw[u]);
-            *reinterpret_cast<uint4*>(hp + c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(hp + a.hplane + c) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            for (int u = 0; u < 4; ++u) {
+              const int c = half * 32 + 8 * k + 2 * u;
+              h16_split2(o[c] * inv, o[c + 1] * inv, hw[u], lw[u]);
+            }
+            *reinterpret_cast<uint4*>(stg + lane * 32 + 4 * (k ^ (lane & 7))) =
+                make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(stg + lane * 32 + 4 * ((4 + k) ^ (lane & 7))) =
+                make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int rr = 4 * q + (lane >> 3);
+            const int c = lane & 7;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 32 + 4 * (c ^ (rr & 7)));
+            if (rr < valid)
+              *reinterpret_cast<uint4*>(a.o_h16 + (c >> 2) * a.hplane + (row0 + rr) * a.hld +
+                                        it.h * kD + half * 32 + (c & 3) * 8) = v;
+          }
+          __syncwarp();
         }
       }
     }
