@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import argparse
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -66,25 +67,34 @@ def compile_one(src: str) -> tuple[str, str]:
 
 
 # Kernels that move registers between warpgroups with setmaxnreg, and the
-# per-thread register count their split assumes (csrc/gemm_tcgen05.cu,
-# csrc/attention_f16.cu: 384 threads launched at 168 registers; the warpgroups
-# then take 56 and 224). A kernel compiled to any other count would make
-# setmaxnreg.inc wait forever.
-SETMAXNREG_KERNELS = {"gemm_tf32x3_kernel": 168, "attention_f16_kernel": 168}
+# per-thread register count their split assumes. csrc/attention_f16.cu: 384
+# threads launched at 168. csrc/gemm_tcgen05.cu: the last template argument
+# (EPI, the number of epilogue warpgroups) sets it: 2 -> 384 threads at 168,
+# 4 -> 640 threads at 96 (EpiCfg there). A kernel compiled to any other count
+# could make setmaxnreg.inc wait forever.
+def expected_registers(mangled: str) -> int | None:
+    if "attention_f16_kernel" in mangled:
+        return 168
+    m = re.search(r"gemm_tf32x3_kernelI(.*?)EEv", mangled)
+    if m:
+        epi = int(re.findall(r"Li(\d+)E", m.group(1) + "E")[-1])
+        return {2: 168, 4: 96}[epi]
+    return None
 
 
 def check_register_split(ptxas_log: str) -> None:
-    current = None
+    current, expected = None, None
     for line in ptxas_log.splitlines():
         if "Compiling entry function" in line:
-            current = next((k for k in SETMAXNREG_KERNELS if k in line), None)
-        elif current and "Used" in line and "registers" in line:
+            current = line.split("'")[1] if "'" in line else line
+            expected = expected_registers(current)
+        elif expected is not None and "Used" in line and "registers" in line:
             used = int(line.split("Used")[1].split("registers")[0])
-            if used != SETMAXNREG_KERNELS[current]:
+            if used != expected:
                 raise RuntimeError(
                     f"{current} compiled to {used} registers per thread; its setmaxnreg split "
-                    f"requires exactly {SETMAXNREG_KERNELS[current]}")
-            current = None
+                    f"requires exactly {expected}")
+            current, expected = None, None
 
 
 def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> str:

@@ -57,17 +57,32 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128;
-constexpr int kEpiWarps = 8;    // two epilogue warpgroups
-constexpr int kStgPitch = 36;   // floats per row of an epilogue transpose buffer
-// 12 warps: warpgroup 0 = TMA producer, MMA issuer, two idle warps; warpgroups
-// 1 and 2 = epilogue. Launched at 168 registers per thread (65536 / 384), then
-// warpgroup 0 gives registers up (kCtrlRegs) and the epilogue warpgroups take
-// them (kEpiRegs): 128 * 56 + 256 * 224 = 384 * 168. build.py checks that ptxas
-// allocated exactly 168 registers to these kernels.
-constexpr int kThreads = 384;
-constexpr uint32_t kCtrlRegs = 56;
-constexpr uint32_t kEpiRegs = 224;
-static_assert(128 * kCtrlRegs + 256 * kEpiRegs == 384 * 168, "register split");
+// Epilogue transpose buffer of one warp: 32 rows x 32 words (pitch 32); the
+// 16-byte chunk q of row r sits at chunk position q ^ (r & 7), so a lane
+// writing its own row and eight lanes reading one row both touch eight
+// different bank groups.
+constexpr int kStgWords = 32 * 32;
+__device__ __forceinline__ int stg_at(int r, int q) { return r * 32 + 4 * (q ^ (r & 7)); }
+// Warpgroup 0 = TMA producer, MMA issuer, two idle warps; warpgroups 1..EPI =
+// epilogue (EPI = 2 or 4). Launched at kLaunchRegs registers per thread
+// (65536 / threads, rounded down to 8), then warpgroup 0 gives registers up
+// (kCtrlRegs) and the epilogue warpgroups take them (kEpiRegs):
+//   EPI 2: 384 threads at 168: 128 * 56 + 256 * 224 = 64512 = 384 * 168
+//   EPI 4: 640 threads at  96: 128 * 56 + 512 * 104 = 60416 <= 640 * 96
+// build.py checks that ptxas allocated exactly kLaunchRegs to each instance.
+// Every compiled configuration uses EPI = 2: four epilogue warpgroups halve
+// each thread's columns but, at 104 registers, spill and ran 12-20 % slower.
+template <int EPI>
+struct EpiCfg {
+  static constexpr int kThreads = 128 * (1 + EPI);
+  static constexpr uint32_t kLaunchRegs = EPI == 2 ? 168 : 96;
+  static constexpr uint32_t kCtrlRegs = 56;
+  static constexpr uint32_t kEpiRegs = EPI == 2 ? 224 : 104;
+  static_assert(EPI == 2 || EPI == 4, "epilogue warpgroups");
+  static_assert(128 * kCtrlRegs + 128 * EPI * kEpiRegs <= kThreads * kLaunchRegs,
+                "register split exceeds the launch allocation");
+  static_assert(kThreads * kLaunchRegs <= 65536, "registers");
+};
 constexpr int kTmemAll = 512;  // TMEM columns: chunk accumulators of BN columns each
 
 // Operand kinds: TF32 pairs; FP16 splits with B's third plane hi*2^11 (one
@@ -76,7 +91,7 @@ constexpr int kTmemAll = 512;  // TMEM columns: chunk accumulators of BN columns
 // stage is one chunk).
 enum OperandKind : int { kKindTF32 = 0, kKindF16 = 1, kKindF16SD = 2 };
 
-template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI = 2>
 struct GemmCfg {
   static constexpr bool F16 = KIND != kKindTF32;
   static constexpr bool SD = KIND == kKindF16SD;
@@ -94,11 +109,12 @@ struct GemmCfg {
   static constexpr int kStageBytes = 2 * kAPlane + kBPlanes * kBPlane;
   // Per epilogue warp: a 32 x 32 transpose buffer (row pitch 36 floats keeps the
   // 16-byte row writes and the transposed reads free of bank conflicts).
-  static constexpr int kStagingBytes = kEpiWarps * 32 * kStgPitch * 4;
+  static constexpr int kStagingBytes = 4 * EPI * kStgWords * 4;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + 1024;
   static constexpr int kNumBufs = kTmemAll / BN;  // chunk accumulators in TMEM
   static constexpr int kTmemCols = kTmemAll;
-  static constexpr int kHalfN = BN / 2;           // columns per epilogue warpgroup
+  static constexpr int kHalfN = BN / EPI;         // columns per epilogue warpgroup
+  static_assert(kHalfN % 32 == 0, "epilogue columns per warpgroup");
   static constexpr int kTileM = PAIR ? 2 * kBM : kBM;
   static constexpr uint32_t kIdesc = F16 ? make_idesc_f16(kTileM, BN) : make_idesc_tf32(kTileM, BN);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -120,60 +136,35 @@ struct GemmCfg {
 // global access instruction covers four whole 128-byte row segments instead of
 // sixteen bytes of 32 different rows.
 // Stores the FP16 split of a warp's 32 x 32 slab (lane i = row m_base + i,
-// values v) as planes base[p * plane + row * ld + col_base ..]: hi, lo * 2^11
-// and, with `third`, hi * 2^11. Through the warp's transpose buffer: words
-// 0-15 of a row hold hi halves, 16-31 lo halves; lanes 0-3 of each group of
-// eight store a row's hi (64 B), lanes 4-7 its lo, four rows per instruction.
+// values v) as planes base[p * plane + row * ld + col_base ..]: hi and
+// lo * 2^11. Through the warp's transpose buffer: chunks 0-3 of a row hold hi
+// halves, 4-7 lo halves; lanes 0-3 of each group of eight store a row's hi
+// (64 B), lanes 4-7 its lo, four rows per instruction.
 __device__ __forceinline__ void h16_slab_store(const float (&v)[32], float* stg, int lane,
                                                int64_t m_base, int64_t M, uint16_t* base,
-                                               int64_t ld, int64_t plane, int64_t col_base,
-                                               bool third) {
+                                               int64_t ld, int64_t plane, int64_t col_base) {
   const int rsub = lane >> 3;
-  const int c4 = (lane & 7) * 4;
-  float* my_row = stg + lane * kStgPitch;
-  uint32_t sw[16];
+  const int q = lane & 7;  // this lane's 16-byte chunk of a row when flushing
 #pragma unroll
   for (int j = 0; j < 32; j += 8) {
     uint32_t hw[4], lw[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      h16_split2(v[j + 2 * t], v[j + 2 * t + 1], hw[t], lw[t]);
-      if (third) {
-        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[t]));
-        const __half2 s2 = __floats2half2_rn(hf.x * kH16LoScale, hf.y * kH16LoScale);
-        sw[j / 2 + t] = *reinterpret_cast<const uint32_t*>(&s2);
-      }
-    }
-    *reinterpret_cast<uint4*>(my_row + j / 2) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(my_row + 16 + j / 2) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    for (int t = 0; t < 4; ++t) h16_split2(v[j + 2 * t], v[j + 2 * t + 1], hw[t], lw[t]);
+    *reinterpret_cast<uint4*>(stg + stg_at(lane, j / 8)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(stg + stg_at(lane, 4 + j / 8)) =
+        make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
   __syncwarp();
-  const int pl = c4 >> 4;          // 0: hi, 1: lo
-  const int hcol = (c4 & 15) * 2;  // first of this lane's eight columns
+  const int pl = q >> 2;         // 0: hi, 1: lo
+  const int hcol = (q & 3) * 8;  // first of this lane's eight columns
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int r = 4 * k + rsub;
     const int64_t mr = m_base + r;
-    const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgPitch + c4);
+    const uint4 t = *reinterpret_cast<const uint4*>(stg + stg_at(r, q));
     if (mr < M) *reinterpret_cast<uint4*>(base + pl * plane + mr * ld + col_base + hcol) = t;
   }
   __syncwarp();
-  if (third) {
-#pragma unroll
-    for (int j = 0; j < 16; j += 4)
-      *reinterpret_cast<uint4*>(my_row + j) = make_uint4(sw[j], sw[j + 1], sw[j + 2], sw[j + 3]);
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int r = 4 * k + rsub;
-      const int64_t mr = m_base + r;
-      if (c4 < 16 && mr < M) {
-        const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgPitch + c4);
-        *reinterpret_cast<uint4*>(base + 2 * plane + mr * ld + col_base + hcol) = t;
-      }
-    }
-    __syncwarp();
-  }
 }
 
 template <bool F16>
@@ -223,7 +214,7 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
     for (int j = 0; j < 32; ++j) v[j] = v[j] * sc;  // exact: a power of two
     if (part < 2) {
       h16_slab_store(v, stg, lane, m_base, a.M, part == 0 ? e.q16 : e.k16, E, a.M * E,
-                     n0 - part * E, false);
+                     n0 - part * E);
       return;
     }
     // V: transposed per (image, head); lanes hold consecutive tokens, so each
@@ -277,8 +268,8 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
                       (!e.out_h16 || a.vec_h16);
   if (staged) {
     const int rsub = lane >> 3;        // row within a group of four
-    const int c4 = (lane & 7) * 4;     // this lane's float4 within a 32-column row
-    float* my_row = stg + lane * kStgPitch;
+    const int q = lane & 7;            // this lane's 16-byte chunk of a 32-column row
+    const int c4 = q * 4;
     if (e.residual != nullptr) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -286,12 +277,12 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
         const int64_t mr = m_base + r;
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
         if (mr < a.M) t = *reinterpret_cast<const float4*>(e.residual + mr * e.ldr + col_base + c4);
-        *reinterpret_cast<float4*>(stg + r * kStgPitch + c4) = t;
+        *reinterpret_cast<float4*>(stg + stg_at(r, q)) = t;
       }
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
-        const float4 t = *reinterpret_cast<const float4*>(my_row + j);
+        const float4 t = *reinterpret_cast<const float4*>(stg + stg_at(lane, j / 4));
         v[j] = t.x + v[j];
         v[j + 1] = t.y + v[j + 1];
         v[j + 2] = t.z + v[j + 2];
@@ -306,7 +297,7 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
       for (int k = 0; k < 8; ++k) {
         const int r = 4 * k + rsub;
         const int64_t mr = m_base + r;
-        const float4 t = *reinterpret_cast<const float4*>(stg + r * kStgPitch + c4);
+        const float4 t = *reinterpret_cast<const float4*>(stg + stg_at(r, q));
         if (mr < a.M) *reinterpret_cast<float4*>(base + mr * ld + col_base + c4) = t;
       }
       __syncwarp();
@@ -314,13 +305,13 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
     if (e.out != nullptr) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(my_row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        *reinterpret_cast<float4*>(stg + stg_at(lane, j / 4)) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       flush(e.out + plane_off, e.ldo);
     }
     if (e.out_pair != nullptr) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(my_row + j) =
+        *reinterpret_cast<float4*>(stg + stg_at(lane, j / 4)) =
             make_float4(tf32_round(v[j]), tf32_round(v[j + 1]), tf32_round(v[j + 2]),
                         tf32_round(v[j + 3]));
       flush(e.out_pair, e.ldp);
@@ -332,12 +323,12 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
         tf32_split(v[j + 1], h, l.y);
         tf32_split(v[j + 2], h, l.z);
         tf32_split(v[j + 3], h, l.w);
-        *reinterpret_cast<float4*>(my_row + j) = l;
+        *reinterpret_cast<float4*>(stg + stg_at(lane, j / 4)) = l;
       }
       flush(e.out_pair + e.pair_plane, e.ldp);
     }
     if (e.out_h16 != nullptr)
-      h16_slab_store(v, stg, lane, m_base, a.M, e.out_h16, e.ldh, e.h16_plane, col_base, false);
+      h16_slab_store(v, stg, lane, m_base, a.M, e.out_h16, e.ldh, e.h16_plane, col_base);
     return;
   }
 
@@ -429,11 +420,12 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
   }
 }
 
-template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI>
+__global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
-  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
+  using Epi = EpiCfg<EPI>;
   constexpr bool F16 = Cfg::F16;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
@@ -463,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < Cfg::kNumBufs; ++b) {
       mbar_init(&chunk_full_bar[b], 1);
-      // one arrival per draining warp (8 per CTA, of both CTAs for a pair)
-      mbar_init(&chunk_empty_bar[b], PAIR ? 16 : 8);
+      // one arrival per draining warp (4 * EPI per CTA, of both CTAs for a pair)
+      mbar_init(&chunk_empty_bar[b], (PAIR ? 2 : 1) * 4 * EPI);
     }
     mbar_init(&mma_done_bar, 1);
     fence_barrier_init();
@@ -492,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 4) {
   // Control warpgroup: gives registers to the epilogue warpgroups.
-  setmaxnreg_dec<kCtrlRegs>();
+  setmaxnreg_dec<Epi::kCtrlRegs>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -656,16 +648,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   } else {
-    setmaxnreg_inc<kEpiRegs>();
+    setmaxnreg_inc<Epi::kEpiRegs>();
     // ------------------------------------------------------------ epilogue
-    // Warps 4-7 and 8-11: warp w reads TMEM lanes [32*(w%4), +32) (one output
-    // row per thread); warpgroup `half` owns columns [half*BN/2, +BN/2).
-    const int half = (warp - 4) >> 2;
+    // Warps 4 .. 4 + 4*EPI - 1: warp w reads TMEM lanes [32*(w%4), +32) (one
+    // output row per thread); epilogue warpgroup `wg` owns columns
+    // [wg*BN/EPI, +BN/EPI).
+    const int wg = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int col0 = half * Cfg::kHalfN;
+    const int col0 = wg * Cfg::kHalfN;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     float* stg = reinterpret_cast<float*>(ring + STAGES * Cfg::kStageBytes) +
-                 (warp - 4) * 32 * kStgPitch;
+                 (warp - 4) * kStgWords;
     int local = 0;
     bool ok = true;
     for (int tile = unit; tile < num_tiles && ok; tile += num_units, ++local) {
@@ -830,9 +823,10 @@ int g_forced_variant = 0;
 // queried yet).
 int g_pair_slots[64] = {};
 
-template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI = 2>
 int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
-  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>;
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
+  constexpr int kThreads = EpiCfg<EPI>::kThreads;
   constexpr bool F16 = Cfg::F16;
   CUtensorMap ta, tb;
   int st = F16 ? make_planes_map(&ta, p.a_h16, p.M, p.Kp, 2, kBM, BK, 1)
@@ -885,7 +879,7 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
     int slots = (dev >= 0 && dev < 64) ? g_pair_slots[dev] : 0;
     if (slots <= 0) {
       cfg.gridDim = dim3(2 * static_cast<unsigned>(device_num_sms() / 2));
-      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>,
+      if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>,
                                          &cfg) != cudaSuccess ||
           slots <= 0) {
         (void)cudaGetLastError();
@@ -894,24 +888,24 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
       if (dev >= 0 && dev < 64) g_pair_slots[dev] = slots;
     }
     cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
-    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>,
+    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>,
                                         ta, tb, a));
     count_launch();
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_num_sms()));
-    gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>
+    gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>
         <<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, a);
     count_launch();
     return cuda_status(cudaGetLastError());
   }
 }
 
-template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR>
+template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI = 2>
 int set_smem_attr() {
-  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>;
-  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR>,
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
+  return cuda_status(cudaFuncSetAttribute(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           Cfg::kSmemBytes));
 }
