@@ -133,6 +133,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // -------------------------------------------------------------- TMA
@@ -405,8 +407,8 @@ int attention_launch(const float* q_pair, int64_t q_ld, int q_col, const float* 
   a.hplane = h16_plane;
   a.err = device_error_word();
   dim3 grid((T + kQ - 1) / kQ, heads, B);
-  attention_tc_kernel<<<grid, kThreadsA, kSmem, s>>>(tq, tk, tvt, a);
-  count_launch();
+  if (int st = launch_kernel(attention_tc_kernel, grid, dim3(kThreadsA), kSmem, s, 1, tq, tk, tvt, a))
+    return st;
   return cuda_status(cudaGetLastError());
 }
 

@@ -202,6 +202,8 @@ __global__ void __launch_bounds__(kThreadsF, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
   const int n_kv = a.n_kv;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp < 4) {
   setmaxnreg_dec<kCtrlRegsF>();
@@ -592,8 +594,9 @@ int attention_f16_launch(const uint16_t* q16, const uint16_t* k16, int64_t ld, c
   a.err = device_error_word();
   if (a.err == nullptr) return VITB200_E_INVALID_ARG;
   const int grid = static_cast<int>(std::min<int64_t>(items, device_num_sms()));
-  attention_f16_kernel<<<grid, kThreadsF, kSmemF, s>>>(tq, tk, tvt, a);
-  count_launch();
+  if (int st = launch_kernel(attention_f16_kernel, dim3(grid), dim3(kThreadsF), kSmemF, s, 1, tq, tk,
+                             tvt, a))
+    return st;
   return cuda_status(cudaGetLastError());
 }
 

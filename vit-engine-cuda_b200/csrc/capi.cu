@@ -3,6 +3,7 @@
 // the kernels on one stream.
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "engine.h"
@@ -92,6 +93,14 @@ int check_ready() {
 
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VITB200_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
 
 int* device_error_word() {
   int st = 0;

@@ -32,6 +32,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch: every kernel of this library is launched
+// allowed to start before the previous grid on its stream has finished. It
+// calls griddep_wait() before its first global-memory access (this returns
+// once the grids it depends on have completed and their writes are visible)
+// and then griddep_launch_dependents(), so the next grid's CTAs may be
+// scheduled as soon as all of this grid's CTAs have started. Without the
+// launch attribute both are no-ops.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void report_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
 }

@@ -24,6 +24,8 @@ inline int grid_for(int64_t work, int threads) {
 // pair[2][rows][ldp] <- TF32 hi/lo of x[rows][cols] (row stride ldx), zero pad.
 __global__ void split_tf32_kernel(const float* __restrict__ x, int64_t rows, int cols,
                                   int64_t ldx, float* __restrict__ pair, int ldp, int vec_in) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int q_per_row = ldp / 4;
   const int64_t total = rows * q_per_row;
   const int64_t plane = rows * ldp;
@@ -58,8 +60,9 @@ int split_tf32_launch(const float* x, int64_t rows, int cols, int64_t ldx, float
   if (reinterpret_cast<uintptr_t>(pair) % 16) return VITB200_E_ALIGNMENT;
   const int vec_in = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 4 == 0);
   const int64_t work = rows * (ldp / 4);
-  split_tf32_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, rows, cols, ldx, pair, ldp, vec_in);
-  count_launch();
+  if (int st_ = launch_kernel(split_tf32_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, 1, x,
+      rows, cols, ldx, pair, ldp, vec_in))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 
@@ -69,6 +72,8 @@ int split_tf32_launch(const float* x, int64_t rows, int cols, int64_t ldx, float
 __global__ void split_f16_kernel(const float* __restrict__ x, int64_t rows, int cols, int64_t ldx,
                                  float scale, uint16_t* __restrict__ out, int64_t ldo,
                                  int nplanes, int* err) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t o_per_row = ldo / 8;
   const int64_t total = rows * o_per_row;
   const int64_t plane = rows * ldo;
@@ -116,9 +121,9 @@ int split_f16_launch(const float* x, int64_t rows, int cols, int64_t ldx, float 
   int* err = device_error_word();
   if (err == nullptr) return VITB200_E_INVALID_ARG;
   const int64_t work = rows * (ldo / 8);
-  split_f16_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, rows, cols, ldx, scale, out, ldo,
-                                                         nplanes, err);
-  count_launch();
+  if (int st_ = launch_kernel(split_f16_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, 1, x,
+      rows, cols, ldx, scale, out, ldo, nplanes, err))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 
@@ -138,6 +143,8 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
     const float* __restrict__ beta, float* __restrict__ y, int64_t ldy, float* __restrict__ yp,
     int64_t pld, int64_t pplane, uint16_t* __restrict__ yh, int64_t hld, int64_t hplane,
     int64_t rows, float eps) {
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int E = 768;
   constexpr int V = E / 128;  // float4 per lane
   const int lane = threadIdx.x & 31;
@@ -206,6 +213,8 @@ __global__ void layernorm_generic_kernel(const float* __restrict__ x, int64_t ld
                                          int64_t ldy, float* __restrict__ yp, int64_t pld,
                                          int64_t pplane, uint16_t* __restrict__ yh, int64_t hld,
                                          int64_t hplane, int64_t rows, int E, float eps) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -256,15 +265,15 @@ int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const floa
   const int threads = 256;
   const int64_t work = rows * 32;
   if (fast) {
-    layernorm768_kernel<<<grid_for(work, threads), threads, 0, s>>>(
-        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, y_h16, h16_ld, h16_plane, rows,
-        eps);
-  count_launch();
+    if (int st_ = launch_kernel(layernorm768_kernel, dim3(grid_for(work, threads)), dim3(threads),
+        0, s, 1, x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, y_h16, h16_ld, h16_plane,
+        rows, eps))
+      return st_;
   } else {
-    layernorm_generic_kernel<<<grid_for(work, threads), threads, 0, s>>>(
-        x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, y_h16, h16_ld, h16_plane, rows,
-        E, eps);
-  count_launch();
+    if (int st_ = launch_kernel(layernorm_generic_kernel, dim3(grid_for(work, threads)),
+        dim3(threads), 0, s, 1, x, ldx, gamma, beta, y, ldy, y_pair, pair_ld, pair_plane, y_h16,
+        h16_ld, h16_plane, rows, E, eps))
+      return st_;
   }
   return cuda_status(cudaGetLastError());
 }
@@ -275,6 +284,8 @@ int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const floa
 // csrc/kernels/patch_embed.cu:29-44 and torch's Conv2d weight layout agree.
 __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, int H, int W,
                                    float* __restrict__ pair) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int gw = W / 16, gh = H / 16;
   const int P = gw * gh;
   const int K = C * 256;
@@ -313,8 +324,9 @@ int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair
     return VITB200_E_ALIGNMENT;
   if (B == 0) return 0;
   const int64_t work = static_cast<int64_t>(B) * (H / 16) * (W / 16) * C * 64;
-  im2col_pair_kernel<<<grid_for(work, 256), 256, 0, s>>>(img, B, C, H, W, pair);
-  count_launch();
+  if (int st_ = launch_kernel(im2col_pair_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, 1,
+      img, B, C, H, W, pair))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 
@@ -325,6 +337,8 @@ int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair
 __global__ void cls_pos_kernel(const float* __restrict__ cls, int64_t cls_stride,
                                const float* __restrict__ pos, const float* __restrict__ patches,
                                float* __restrict__ out, int B, int P, int E) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int T = P + 1;
   const int64_t rows = patches ? static_cast<int64_t>(B) * T : B;
   const int64_t total = rows * E;
@@ -350,9 +364,9 @@ int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const
   if (B < 0 || P < 0 || E <= 0 || !cls || !pos || !out) return VITB200_E_INVALID_ARG;
   if (B == 0) return 0;
   const int64_t rows = patches ? static_cast<int64_t>(B) * (P + 1) : B;
-  cls_pos_kernel<<<grid_for(rows * E, 256), 256, 0, s>>>(cls, cls_stride, pos, patches, out, B,
-                                                          P, E);
-  count_launch();
+  if (int st_ = launch_kernel(cls_pos_kernel, dim3(grid_for(rows * E, 256)), dim3(256), 0, s, 1,
+      cls, cls_stride, pos, patches, out, B, P, E))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 
@@ -365,6 +379,8 @@ int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const
 __global__ void split_transpose_v_kernel(const float* __restrict__ v, int64_t ldv, int T,
                                          int heads, int T4, float* __restrict__ vt,
                                          int64_t vt_plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float tile[32][33];
   const int bh = blockIdx.z;
   const int b = bh / heads, h = bh - (bh / heads) * heads;
@@ -395,8 +411,9 @@ int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int head
   const int T4 = (T + 3) / 4 * 4;
   const int64_t plane = static_cast<int64_t>(B) * heads * 64 * T4;
   dim3 grid((T + 31) / 32, 2, B * heads);
-  split_transpose_v_kernel<<<grid, dim3(32, 8), 0, s>>>(v, ldv, T, heads, T4, vt_pair, plane);
-  count_launch();
+  if (int st_ = launch_kernel(split_transpose_v_kernel, dim3(grid), dim3(dim3(32, 8)), 0, s, 1, v,
+      ldv, T, heads, T4, vt_pair, plane))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 
@@ -406,6 +423,8 @@ int split_transpose_v_launch(const float* v, int64_t ldv, int B, int T, int head
 __global__ void split_transpose_v_f16_kernel(const float* __restrict__ v, int64_t ldv, int T,
                                              int heads, int T8, float scale,
                                              uint16_t* __restrict__ vt, int64_t plane, int* err) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float tile[32][33];
   const int bh = blockIdx.z;
   const int b = bh / heads, h = bh - (bh / heads) * heads;
@@ -442,9 +461,9 @@ int split_transpose_v_f16_launch(const float* v, int64_t ldv, int B, int T, int 
   const int T8 = (T + 7) / 8 * 8;
   const int64_t plane = static_cast<int64_t>(B) * heads * 64 * T8;
   dim3 grid((T + 31) / 32, 2, B * heads);
-  split_transpose_v_f16_kernel<<<grid, dim3(32, 8), 0, s>>>(v, ldv, T, heads, T8, scale, vt16,
-                                                            plane, err);
-  count_launch();
+  if (int st_ = launch_kernel(split_transpose_v_f16_kernel, dim3(grid), dim3(dim3(32, 8)), 0, s,
+      1, v, ldv, T, heads, T8, scale, vt16, plane, err))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 
@@ -452,6 +471,8 @@ int split_transpose_v_f16_launch(const float* v, int64_t ldv, int B, int T, int 
 // With an empty reduction the product is 0; only the epilogue remains
 // (bias, GELU, residual), matching the reference CuTe kernel's K=0 behaviour.
 __global__ void gemm_k0_kernel(int64_t M, int N, GemmEpilogue e) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t total = M * N;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -478,8 +499,9 @@ __global__ void gemm_k0_kernel(int64_t M, int N, GemmEpilogue e) {
 
 int gemm_k0_launch(const GemmProblem& p, cudaStream_t s) {
   if (p.epi.mode != kModePlain) return VITB200_E_UNSUPPORTED;
-  gemm_k0_kernel<<<grid_for(p.M * p.N, 256), 256, 0, s>>>(p.M, p.N, p.epi);
-  count_launch();
+  if (int st_ = launch_kernel(gemm_k0_kernel, dim3(grid_for(p.M * p.N, 256)), dim3(256), 0, s, 1,
+      p.M, p.N, p.epi))
+    return st_;
   return cuda_status(cudaGetLastError());
 }
 

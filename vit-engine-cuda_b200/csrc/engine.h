@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace vitb200 {
 
 // Row/column mapping of a GEMM epilogue.
@@ -145,5 +147,41 @@ void count_launch();
 
 // Converts a CUDA error to a status (0 stays 0).
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? 0 : static_cast<int>(e); }
+
+// Whether kernels are launched with programmatic stream serialization (see
+// griddep_wait in common.cuh); on unless the environment sets VITB200_PDL=0.
+bool pdl_enabled();
+
+// Launches `kernel` on `s` with the library's launch attributes: programmatic
+// stream serialization (when enabled) and, for cluster_x > 1, a cluster of
+// cluster_x CTAs. Counts the launch; returns a vitb200 status code.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                  unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const int st = cuda_status(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  count_launch();
+  return st;
+}
 
 }  // namespace vitb200

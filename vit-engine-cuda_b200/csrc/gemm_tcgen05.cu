@@ -477,6 +477,8 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   const int num_tiles = args.num_tiles;
   const int num_kb = args.num_kb;
@@ -887,17 +889,16 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
       }
       if (dev >= 0 && dev < 64) g_pair_slots[dev] = slots;
     }
-    cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
-    st = cuda_status(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>,
-                                        ta, tb, a));
-    count_launch();
+    const dim3 grid(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
+    st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
+                       dim3(kThreads), Cfg::kSmemBytes, s, 2, ta, tb, a);
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, device_num_sms()));
-    gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>
-        <<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, a);
-    count_launch();
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, device_num_sms())));
+    st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
+                       dim3(kThreads), Cfg::kSmemBytes, s, 1, ta, tb, a);
+    if (st) return st;
     return cuda_status(cudaGetLastError());
   }
 }

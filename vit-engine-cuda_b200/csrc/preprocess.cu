@@ -52,6 +52,8 @@ __device__ __forceinline__ void aa_window(float s, int i, int in_size, int& lo, 
 
 __global__ void preprocess_kernel(const uint8_t* __restrict__ img, float* __restrict__ out,
                                   PreArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t per_img = static_cast<int64_t>(a.crop) * a.crop;
   const int64_t total = per_img * a.B;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -131,7 +133,8 @@ extern "C" int vitb200_preprocess(const uint8_t* images, int B, int H, int W, in
     return st;
   const int64_t work = static_cast<int64_t>(B) * crop * crop;
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(sms) * 8));
-  preprocess_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(images, out, a);
-  count_launch();
+  if (int st = launch_kernel(preprocess_kernel, dim3(grid), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), 1, images, out, a))
+    return st;
   return cuda_status(cudaGetLastError());
 }
