@@ -174,3 +174,18 @@ def test_out_of_range_block_falls_back_to_tf32(cuda):
         out = model(img.to(cuda)).double().cpu()
     assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
     assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
+def test_streamed_inference_matches_eager(cuda):
+    """Host-resident batches through vit_cuda.StreamedInference (copy of batch
+    i+1 overlapping the forward of batch i) give the eager logits bitwise."""
+    import vit_cuda
+    state = synthetic_state_dict(seed=3, img_size=224)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    batches = [synthetic_images(3, 224, seed=20 + i).pin_memory() for i in range(5)]
+    run = vit_cuda.StreamedInference(model, (3, 3, 224, 224))
+    outs = [run(x) for x in batches]
+    torch.cuda.current_stream().synchronize()
+    with torch.no_grad():
+        for x, o in zip(batches, outs):
+            torch.testing.assert_close(o, model(x.to(cuda)).cpu(), atol=0, rtol=0)

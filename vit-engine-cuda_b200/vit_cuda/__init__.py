@@ -10,6 +10,7 @@ from .library import (classifier_forward, flash_attn_2, gemm_bias, layernorm_for
                       mlp_forward, patch_embed, pos_encoding, qkv_proj)
 from ._lib import VitB200Error, device_error
 from .model import ViTBlockCUDA, ViTCUDA
+from .pipeline import StreamedInference
 from .preprocess import preprocess
 
 __all__ = [
@@ -26,4 +27,5 @@ __all__ = [
     "VitB200Error",
     "device_error",
     "preprocess",
+    "StreamedInference",
 ]
