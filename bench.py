@@ -56,6 +56,7 @@ CONFIGS = {
     # name: (images per GPU per step, image size)
     "bs256_224": (256, 224),   # bs256 on one B200
     "bs512_384": (512, 384),   # BASELINE configs[4] per-GPU shard (B=4096 over 8 GPUs)
+    "bs1_224": (1, 224),       # BASELINE configs[0] shape (batch-1 latency studies)
 }
 GFLOP_PER_IMG = {224: 35.1277, 384: 110.9687}
 # Block GEMMs as the model launches them: (N, K, epilogue, FP16-split output).
