@@ -38,6 +38,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from datetime import timedelta
 
@@ -96,41 +97,62 @@ def emit(obj):
 
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """nvidia-smi samples every 50 ms, read on a thread with their arrival
+    times; ``start()`` waits for the first sample (the tool takes a moment to
+    come up) and marks the timed region's start, ``stop()`` its end, and only
+    samples inside the region count."""
 
     def __init__(self, device_index: int):
         self.proc = None
-        self.lines = []
+        self.samples = []  # (monotonic time, fields)
+        self.t0 = self.t1 = None
+        self.first = threading.Event()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={SMI_FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(device_index)],
+                 "-lms", "50", "-i", str(device_index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.samples.append((time.monotonic(), [c.strip() for c in ln.split(",")]))
+                self.first.set()
+
+    def start(self):
+        if self.proc is not None:
+            self.first.wait(timeout=15)
+        self.t0 = time.monotonic()
 
     def stop(self):
+        self.t1 = time.monotonic()
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
+                    "samples": 0}
+        time.sleep(0.1)  # the sample taken at the region's end
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
-        rows = [[c.strip() for c in ln.split(",")] for ln in out.splitlines() if ln.strip()]
+            self.proc.wait()
+        self.reader.join(timeout=5)
         sm, smax, reasons = [], None, set()
-        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
-                 "sw_power_cap"]
-        for r in rows:
-            if len(r) < 9:
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for t, r in list(self.samples):
+            if len(r) < 9 or not (self.t0 <= t <= self.t1 + 0.06):
                 continue
             try:
                 sm.append(float(r[1]))
                 smax = float(r[2])
             except ValueError:
                 continue
-            for name, val in zip(names[1:], r[5:9]):
+            for name, val in zip(names, r[5:9]):
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
@@ -333,6 +355,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in
                               os.environ else local_rank)
+        clocks.start()
         n0 = _lib.lib.vitb200_launch_count()
         ms = timed(step_device, args.steps, world, dev)
         launches = _lib.lib.vitb200_launch_count() - n0

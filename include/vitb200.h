@@ -91,6 +91,27 @@ uint64_t vitb200_launch_count(void);
  * previous setting. For tuning and tests; process-wide. */
 int vitb200_set_gemm_variant(int variant);
 
+/* Split-K of small single-CTA GEMM launches (on by default). When the output
+ * tile grid fills at most half the SMs (e.g. the block GEMMs of a batch-1
+ * forward, M = 197 rows), the launch splits K into d <= 8 equal parts over a
+ * thread-block cluster of d CTAs per tile; the other CTAs leave their fp32
+ * partial tiles in their shared memory and the cluster's first CTA adds them
+ * in split order over distributed shared memory (deterministic) and writes the
+ * tile. With split-K off, an image's logits are bitwise identical whatever
+ * batch it is in, among batches of fewer than 1024 token rows (the block GEMMs
+ * then all use single-CTA tiles with the same K chunks); with it on they agree
+ * to FP32 rounding. No counterpart in the reference (one CTA per 32x32 output
+ * tile there). Affects launches made after the call (a captured CUDA graph
+ * keeps the setting it was captured with). Returns the previous setting;
+ * process-wide. */
+int vitb200_set_split_k(int enable);
+
+/* The tile configuration (*variant, as in vitb200_set_gemm_variant) and the K
+ * split (*ksplit, 1 = none) that a GEMM of M x K by K x N (f16 = 1: FP16-split
+ * operands, 0: TF32 pairs) launched now on the current device would use.
+ * Either output may be NULL. For diagnostics and tests. */
+int vitb200_gemm_plan(int64_t M, int K, int N, int f16, int* variant, int* ksplit);
+
 /* ---- TF32 split -------------------------------------------------------- */
 
 /* Writes the TF32 pair of x[rows][cols] (row stride ldx floats) into

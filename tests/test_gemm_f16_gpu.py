@@ -145,3 +145,64 @@ def test_gemm_f16_bad_arguments(vlib, cuda):
     # misaligned operand
     assert lib.vitb200_gemm_f16(a.data_ptr() + 2, a.data_ptr(), 1.0, None, None, y.data_ptr(), 4,
                                 None, 4, 8, 4, vlib.EPI_NONE, s) == vlib.E_ALIGNMENT
+
+
+# Batch-1 ViT-B/16 block GEMMs (M = 197 rows: qkv, proj, fc2) and an odd K
+# (620: 10 K blocks of 64 for the FP16 kind, 20 of 32 for TF32, the last one
+# ragged in both) whose tile grids fill few SMs, so their launches split K;
+# fc1 (96 tiles of 64 columns, too many to split) forced onto 128-wide tiles,
+# which split.
+SPLIT_K_CASES = [((197, 768, 2304), None), ((197, 768, 768), None), ((197, 3072, 768), None),
+                 ((130, 620, 200), None), ((197, 768, 3072), "bn128")]
+
+
+@pytest.mark.parametrize("kind", ["f16", "tf32"])
+@pytest.mark.parametrize("shape,forced", SPLIT_K_CASES)
+@pytest.mark.parametrize("epi", ["bias", "gelu", "resid"])
+def test_split_k(vlib, cuda, kind, shape, forced, epi):
+    """Small launches split K over a cluster of CTAs per output tile (partial
+    tiles added in split order over distributed shared memory). FP32 parity
+    with split-K on and off; on, results repeat bitwise, and (for K >= 768)
+    differ in the last bits from the unsplit sums, which shows the split ran."""
+    torch.manual_seed(5)
+    m, k, n = shape
+    variant = {None: 0, "bn128": 10 if kind == "f16" else 1}[forced]
+    old_variant = vlib.lib.vitb200_set_gemm_variant(variant)
+    try:
+        _, ksplit = vlib.gemm_plan(m, k, n, kind == "f16")
+        assert ksplit > 1
+        x = torch.randn(m, k, device=cuda)
+        w = torch.randn(n, k, device=cuda) * 0.05
+        bias = torch.randn(n, device=cuda)
+        res = torch.randn(m, n, device=cuda) if epi == "resid" else None
+
+        def run():
+            if kind == "f16":
+                return run_f16(vlib, x, w, bias, res, epi)
+            return run_gemm(vlib, x, w, bias, res, epi)
+
+        y1, y2 = run(), run()
+        old = vlib.lib.vitb200_set_split_k(0)
+        try:
+            assert vlib.gemm_plan(m, k, n, kind == "f16")[1] == 1
+            y0 = run()
+        finally:
+            vlib.lib.vitb200_set_split_k(old)
+    finally:
+        vlib.lib.vitb200_set_gemm_variant(old_variant)
+    assert old == 1
+    assert torch.equal(y1, y2)
+    check_fp32_parity(y1, x, w, bias, res, epi)
+    check_fp32_parity(y0, x, w, bias, res, epi)
+    if k >= 768:
+        assert not torch.equal(y0, y1)
+    assert vlib.device_error(clear=True) == 0
+
+
+def test_large_launches_do_not_split(vlib, cuda):
+    """Batch-256 shapes run on CTA pairs, unsplit; so does any M >= 1024."""
+    for f16 in (True, False):
+        for k, n in ((768, 2304), (768, 768), (768, 3072), (3072, 768)):
+            v, d = vlib.gemm_plan(50432, k, n, f16)
+            assert d == 1 and v == (15 if f16 else 6)
+        assert vlib.gemm_plan(1024, 768, 768, f16)[1] == 1

@@ -173,6 +173,16 @@ uint64_t vitb200_launch_count(void) { return g_launches.load(std::memory_order_r
 
 int vitb200_set_gemm_variant(int variant) { return gemm_set_variant(variant); }
 
+int vitb200_set_split_k(int enable) { return gemm_set_split_k(enable); }
+
+int vitb200_gemm_plan(int64_t M, int K, int N, int f16, int* variant, int* ksplit) {
+  VITB200_GUARD_BEGIN
+  if (M <= 0 || K <= 0 || N <= 0) return VITB200_E_INVALID_ARG;
+  const int pad = f16 ? 8 : 4;
+  return gemm_plan(M, N, (K + pad - 1) / pad * pad, f16, variant, ksplit);
+  VITB200_GUARD_END
+}
+
 int vitb200_split_tf32(const float* x, int64_t rows, int cols, int64_t ldx, float* pair, int ldp,
                        void* stream) {
   VITB200_GUARD_BEGIN

@@ -22,6 +22,7 @@ enum DeviceError : int {
   kErrWaitAccEmpty = 4, // MMA issuer waited too long for a drained accumulator
   kErrDrain = 5,        // error path: in-flight copies did not land in time
   kErrF16Range = 6,     // a value outside the FP16-split range reached a split
+  kErrWaitSplit = 7,    // split-K leader waited too long for the other CTAs' partial sums
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 1000000000ull;  // 1 s
@@ -435,6 +436,55 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
+}
+
+// Bounded wait, with acquire at cluster scope, on a barrier of this CTA that
+// threads of other CTAs of the cluster arrive on (mbar_arrive_cluster): their
+// writes before the arrival are visible to this thread afterwards.
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity, int* err,
+                                                      int code) {
+  const uint32_t addr = smem_addr(bar);
+  if (mbar_try_wait_acq_cluster(addr, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t polls = 0;
+  while (true) {
+    if (mbar_try_wait_acq_cluster(addr, parity)) return true;
+    if ((++polls & 63u) == 0) {
+      if (error_raised(err)) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        report_error(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+// 16-byte load from another CTA's shared memory (shared::cluster address).
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+// Orders this thread's earlier async-proxy (TMA / tensor core) accesses of
+// shared memory with its later generic ones.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // 3-D tiled load into this CTA's shared memory whose completion is counted on

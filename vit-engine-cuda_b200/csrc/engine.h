@@ -89,6 +89,12 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t stream);
 int gemm_prepare_device();
 // Forces one tile configuration (0 = automatic choice); returns the old value.
 int gemm_set_variant(int v);
+// Switches split-K of later small single-CTA launches on / off; returns the
+// old setting.
+int gemm_set_split_k(int enable);
+// Tile configuration (variant) and K split a launch of this shape would use
+// on the current device.
+int gemm_plan(int64_t M, int N, int Kp, int f16, int* variant, int* ksplit);
 
 // Device error word of the current device (resolved once per device).
 int* device_error_word();

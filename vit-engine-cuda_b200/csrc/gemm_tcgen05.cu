@@ -45,7 +45,9 @@ struct GemmArgs {
   int num_n_tiles;
   int num_tiles;
   int num_kb;
-  int num_chunks;  // chunks per tile
+  int num_chunks;  // chunks per work unit
+  int ksplit;      // K splits per output tile: a cluster of ksplit CTAs, one split each
+  int kb_per;      // K blocks per work unit (num_kb / ksplit)
   int vec_out;     // fp32 output rows are 16-byte aligned (float4 stores)
   int vec_pair;    // pair rows are 16-byte aligned
   int vec_res;     // residual rows are 16-byte aligned
@@ -123,6 +125,8 @@ struct GemmCfg {
   static_assert((kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols >= 32 && kTmemCols <= 512,
                 "TMEM columns must be a power of two in [32, 512]");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+  // split-K partial sums of a CTA (128 x BN fp32) fit in its stage ring
+  static_assert(128 * BN * 4 <= STAGES * kStageBytes, "split-K partials");
   static_assert(CHUNK_KB >= 1, "chunk");
   static_assert(!SD || CHUNK_KB == 1, "scale-input-d needs one stage per chunk");
 };
@@ -433,6 +437,7 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
   __shared__ __align__(8) uint64_t chunk_full_bar[Cfg::kNumBufs];
   __shared__ __align__(8) uint64_t chunk_empty_bar[Cfg::kNumBufs];
   __shared__ __align__(8) uint64_t mma_done_bar;
+  __shared__ __align__(8) uint64_t split_bar[4 * EPI];  // split-K: other CTAs' partials ready
   __shared__ uint32_t tmem_base_slot;
 
   const int warp = threadIdx.x >> 5;
@@ -459,11 +464,16 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       mbar_init(&chunk_empty_bar[b], (PAIR ? 2 : 1) * 4 * EPI);
     }
     mbar_init(&mma_done_bar, 1);
+    if (!PAIR && args.ksplit > 1) {
+      // one arrival per lane of each other CTA's slab warp
+      for (int i = 0; i < 4 * EPI; ++i) mbar_init(&split_bar[i], 32 * (args.ksplit - 1));
+    }
     fence_barrier_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
   }
-  if constexpr (PAIR) cluster_sync_all();  // peer barriers initialised before any remote use
+  // Peer barriers initialised before any remote use (CTA pair, split-K cluster).
+  if (PAIR || args.ksplit > 1) cluster_sync_all();
   if (warp == 1) {
     if constexpr (PAIR) {
       tmem_alloc_pair(&tmem_base_slot, Cfg::kTmemCols);
@@ -481,8 +491,11 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
   griddep_launch_dependents();
 
   const int num_tiles = args.num_tiles;
-  const int num_kb = args.num_kb;
   const int num_chunks = args.num_chunks;
+  // Work unit w: output tile w / ksplit, K blocks [(w % ksplit) * kb_per, +kb_per).
+  const int ksplit = args.ksplit;
+  const int kb_per = args.kb_per;
+  const int num_work = num_tiles * ksplit;
 
   if (warp < 4) {
   // Control warpgroup: gives registers to the epilogue warpgroups.
@@ -494,12 +507,14 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       uint32_t phase = 0;
       int64_t issued = 0;
       bool ok = true;
-      for (int tile = unit; tile < num_tiles && ok; tile += num_units) {
+      for (int w = unit; w < num_work && ok; w += num_units) {
+        const int tile = w / ksplit;
+        const int kb0 = (w - tile * ksplit) * kb_per;
         const int m_blk = tile / args.num_n_tiles;
         const int n_blk = tile - m_blk * args.num_n_tiles;
         const int a_row = m_blk * Cfg::kTileM + static_cast<int>(rank) * kBM;
         const int b_row = n_blk * BN + static_cast<int>(rank) * Cfg::kBRows;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb0 + kb_per; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -554,11 +569,11 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
           umma_commit(bar);
         }
       };
-      for (int tile = unit; tile < num_tiles && ok; tile += num_units, ++local) {
-        for (int kb = 0; kb < num_kb; ++kb) {
+      for (int w = unit; w < num_work && ok; w += num_units, ++local) {
+        for (int kb = 0; kb < kb_per; ++kb) {  // relative to the work unit's first K block
           const int j = kb / CHUNK_KB;
           const bool chunk_first = (kb - j * CHUNK_KB) == 0;
-          const bool chunk_last = (kb - j * CHUNK_KB) == CHUNK_KB - 1 || kb == num_kb - 1;
+          const bool chunk_last = (kb - j * CHUNK_KB) == CHUNK_KB - 1 || kb == kb_per - 1;
           int buf;
           uint32_t use;
           chunk_slot<Cfg::kNumBufs>(local, j, num_chunks, buf, use);
@@ -663,7 +678,9 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
                  (warp - 4) * kStgWords;
     int local = 0;
     bool ok = true;
-    for (int tile = unit; tile < num_tiles && ok; tile += num_units, ++local) {
+    for (int w = unit; w < num_work && ok; w += num_units, ++local) {
+      const int tile = w / ksplit;
+      const int split = w - tile * ksplit;
       const int m_blk = tile / args.num_n_tiles;
       const int n_blk = tile - m_blk * args.num_n_tiles;
       float sum[Cfg::kHalfN];
@@ -697,6 +714,43 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
         }
       }
       if (!ok) break;
+      if constexpr (!PAIR) {
+        if (ksplit > 1) {
+          // Split K over a cluster of ksplit CTAs, one work unit each (split =
+          // cluster rank). The others leave their partial sums in their own
+          // stage ring, idle now that their last MMA has completed; the leader
+          // (split 0) adds them in split order over distributed shared memory
+          // (deterministic) and finishes the tile. Layout [slab][c / 4][lane]
+          // of float4: each warp access is 512 contiguous bytes.
+          const int slab = warp - 4;
+          float4* part = reinterpret_cast<float4*>(ring) + slab * (Cfg::kHalfN / 4) * 32 + lane;
+          if (split != 0) {
+            fence_proxy_async_smem();
+#pragma unroll
+            for (int c = 0; c < Cfg::kHalfN; c += 4)
+              part[(c / 4) * 32] = make_float4(sum[c], sum[c + 1], sum[c + 2], sum[c + 3]);
+            mbar_arrive_cluster(mapa_shared(smem_addr(&split_bar[slab]), 0));
+            continue;
+          }
+          const bool got = mbar_wait_acq_cluster(&split_bar[slab], 0, err, kErrWaitSplit);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          const uint32_t part_addr = smem_addr(part);
+          for (int sp = 1; sp < ksplit; ++sp) {
+            const uint32_t src = mapa_shared(part_addr, static_cast<uint32_t>(sp));
+#pragma unroll
+            for (int c = 0; c < Cfg::kHalfN; c += 4) {
+              const float4 t = ld_shared_cluster_f4(src + static_cast<uint32_t>(c / 4) * 512u);
+              sum[c] += t.x;
+              sum[c + 1] += t.y;
+              sum[c + 2] += t.z;
+              sum[c + 3] += t.w;
+            }
+          }
+        }
+      }
       // Rows of this warp: m_base .. m_base + 31 (lane i holds row m_base + i).
       const int64_t m_base = static_cast<int64_t>(m_blk) * Cfg::kTileM +
                              static_cast<int64_t>(rank) * kBM + quarter * 32;
@@ -719,7 +773,9 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync_all();  // neither CTA releases TMEM / exits early
+  // Pair: neither CTA releases TMEM / exits early. Split-K: no CTA exits while
+  // the leader may still read its partial sums.
+  if (PAIR || args.ksplit > 1) cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -817,16 +873,67 @@ constexpr Variant kVariants[] = {
     {1, 256, 32, 4, 4, 1},  {1, 256, 64, 2, 1, 1}, {1, 128, 64, 2, 1, 0}, {1, 256, 64, 2, 4, 1},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+struct GemmPlan {
+  int variant;  // index into kVariants
+  int ksplit;   // K splits (clusters of ksplit CTAs per tile; 1 = none)
+};
 constexpr int kPairVariant = 6;
 constexpr int kF16PairVariant = 15;
 int g_forced_variant = 0;
+// Split-K of small single-CTA launches (on unless switched off).
+int g_split_k = 1;
 
 // Cluster-of-two slots that fit on the device at once, per device (0 = not
 // queried yet).
 int g_pair_slots[64] = {};
 
+constexpr int kMaxSplit = 8;  // portable cluster size
+
+// Clusters of `d` CTAs of this kernel that fit on the device at once (cached
+// per device and d; 0 when the query fails).
+template <typename Kernel>
+int split_cluster_slots(Kernel kernel, int smem, int threads, int d) {
+  static int cache[64][kMaxSplit + 1] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  int& slot = cache[dev][d];
+  if (slot == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(d);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(d * (device_num_sms() / d)));
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = -1;
+    }
+    slot = n;
+  }
+  return slot > 0 ? slot : 0;
+}
+
+// Whether a single-CTA launch of `tiles` output tiles over num_kb K blocks can
+// split K d ways: d divides num_kb, tiles * d CTAs fit in one wave of SMs and
+// all `tiles` clusters of d CTAs are resident at once.
+template <typename Kernel>
+bool split_fits(Kernel kernel, int smem, int threads, int64_t tiles, int num_kb, int d) {
+  if (d == 1) return true;
+  if (d < 1 || d > kMaxSplit || num_kb % d != 0 || tiles * d > device_num_sms()) return false;
+  return split_cluster_slots(kernel, smem, threads, d) >= tiles;
+}
+
 template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI = 2>
-int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
+int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
   using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
   constexpr int kThreads = EpiCfg<EPI>::kThreads;
   constexpr bool F16 = Cfg::F16;
@@ -848,7 +955,12 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
   if (tiles > 0x7fffffff) return VITB200_E_UNSUPPORTED;
   a.num_tiles = static_cast<int>(tiles);
   a.num_kb = (p.Kp + BK - 1) / BK;
-  a.num_chunks = (a.num_kb + CHUNK_KB - 1) / CHUNK_KB;
+  // Small problems (batch-1 latency) split K over clusters of CTAs so that
+  // more SMs stream the operands (single-CTA tiles only).
+  if (ksplit < 1 || (PAIR && ksplit != 1) || a.num_kb % ksplit != 0) return VITB200_E_INVALID_ARG;
+  a.ksplit = ksplit;
+  a.kb_per = a.num_kb / ksplit;
+  a.num_chunks = (a.kb_per + CHUNK_KB - 1) / CHUNK_KB;
   const GemmEpilogue& e = p.epi;
   a.vec_out = (e.out != nullptr) && (reinterpret_cast<uintptr_t>(e.out) % 16 == 0) &&
               (e.ldo % 4 == 0) && (e.mode != kModeSplit3 || e.split_plane % 4 == 0);
@@ -895,9 +1007,12 @@ int launch_variant(const GemmProblem& p, int* err, cudaStream_t s) {
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
-    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, device_num_sms())));
+    // Split: exactly one CTA per (tile, split), clusters of ksplit CTAs.
+    const dim3 grid(static_cast<unsigned>(
+        a.ksplit > 1 ? tiles * a.ksplit : std::min<int64_t>(tiles, device_num_sms())));
     st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
-                       dim3(kThreads), Cfg::kSmemBytes, s, 1, ta, tb, a);
+                       dim3(kThreads), Cfg::kSmemBytes, s, static_cast<unsigned>(a.ksplit), ta,
+                       tb, a);
     if (st) return st;
     return cuda_status(cudaGetLastError());
   }
@@ -911,31 +1026,101 @@ int set_smem_attr() {
                                           Cfg::kSmemBytes));
 }
 
-int pick_variant(int64_t M, int N, bool f16) {
-  // Large problems: 256 x 128 tiles on CTA pairs (each SM streams half of B,
-  // so operand traffic per FLOP matches a 256-wide tile). Small ones (batch-1
-  // latency): the single-CTA tile width that minimises (waves of tiles) x
-  // (tile width); a partial last wave costs a full one.
-  const int sms = device_num_sms();
-  if (M >= 1024) return f16 ? kF16PairVariant : kPairVariant;
-  const int64_t m_tiles = (M + kBM - 1) / kBM;
-  int best = f16 ? 10 : 1;
-  int64_t best_cost = -1;
-  const int cands[2] = {f16 ? 10 : 1, f16 ? 11 : 3};  // BN = 128, 64
-  for (int c : cands) {
-    const int bn = kVariants[c].bn;
-    const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
-    const int64_t waves = (tiles + sms - 1) / sms;
-    const int64_t cost = waves * bn;
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = c;
-    }
+// A tile configuration as a type, for visitors over the variant table.
+template <int KIND_, int BN_, int BK_, int STAGES_, int CHUNK_KB_, bool PAIR_>
+struct VariantT {
+  static constexpr int KIND = KIND_, BN = BN_, BK = BK_, STAGES = STAGES_, CHUNK_KB = CHUNK_KB_;
+  static constexpr bool PAIR = PAIR_;
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, 2>;
+  static constexpr auto kernel() { return gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, 2>; }
+};
+
+// Calls f(VariantT<...>{}) for variant v (1 .. kNumVariants - 1); the order
+// matches kVariants.
+template <typename F>
+int with_variant(int v, F&& f) {
+  switch (v) {
+    case 1: return f(VariantT<kKindTF32, 128, 32, 2, 4, false>{});
+    case 2: return f(VariantT<kKindTF32, 128, 16, 5, 8, false>{});
+    case 3: return f(VariantT<kKindTF32, 64, 32, 3, 4, false>{});
+    case 4: return f(VariantT<kKindTF32, 128, 32, 2, 2, false>{});
+    case 5: return f(VariantT<kKindTF32, 256, 16, 3, 8, false>{});
+    case 6: return f(VariantT<kKindTF32, 256, 32, 2, 4, true>{});
+    case 7: return f(VariantT<kKindTF32, 256, 16, 5, 8, true>{});
+    case 8: return f(VariantT<kKindTF32, 256, 16, 5, 16, true>{});
+    case 9: return f(VariantT<kKindF16, 256, 64, 2, 2, true>{});
+    case 10: return f(VariantT<kKindF16, 128, 64, 2, 2, false>{});
+    case 11: return f(VariantT<kKindF16, 64, 64, 3, 2, false>{});
+    case 12: return f(VariantT<kKindF16, 256, 32, 4, 4, true>{});
+    case 13: return f(VariantT<kKindF16SD, 256, 64, 2, 1, true>{});
+    case 14: return f(VariantT<kKindF16SD, 128, 64, 2, 1, false>{});
+    case 15: return f(VariantT<kKindF16, 256, 64, 2, 4, true>{});
+    default: return VITB200_E_UNSUPPORTED;
   }
-  return best;
+}
+
+// Launch cost model for small problems, in units of about 40 ps. A CTA's K
+// loop is latency-bound (a few stages of operands in flight per SM), so a K
+// block costs about (stage bytes) / (stages): measured on B200 at M = 197,
+// 0.75 us for 64-wide F16 tiles (3 stages of 56 KB), 1.5 us for 128-wide ones
+// (2 of 80 KB). A split adds the cluster barriers and the leader's reads of
+// the partial tiles over distributed shared memory (under 1 us at d = 4).
+constexpr int64_t kSplitFixedCost = 12 * 1024;
+constexpr int64_t kSplitPerCtaCost = 5 * 1024;
+
+// Tile configuration and K split of a launch. Large problems (M >= 1024):
+// 256 x 128 tiles on CTA pairs (each SM streams half of B, so operand traffic
+// per FLOP matches a 256-wide tile), no split. Small ones (batch-1 latency):
+// among the single-CTA tile widths and the K splits that fit, the cheapest by
+// the model above: (waves) x (K blocks per split) x (cost of a K block) + the
+// split's cost; a partial last wave costs a full one.
+GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
+  GemmPlan plan{0, 1};
+  const int forced = g_forced_variant;
+  const bool use_forced = forced != 0 && (kVariants[forced].f16 != 0) == f16;
+  if (!use_forced && M >= 1024) {
+    plan.variant = f16 ? kF16PairVariant : kPairVariant;
+    return plan;
+  }
+  const int sms = device_num_sms();
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  const int cands_f16[2] = {10, 11}, cands_tf32[2] = {1, 3};  // BN = 128, 64
+  const int* cands = f16 ? cands_f16 : cands_tf32;
+  int64_t best_cost = -1;
+  for (int i = 0; i < (use_forced ? 1 : 2); ++i) {
+    const int v = use_forced ? forced : cands[i];
+    with_variant(v, [&](auto t) {
+      using T = decltype(t);
+      const int64_t tiles = (T::PAIR ? (M + 2 * kBM - 1) / (2 * kBM) : m_tiles) *
+                            ((N + T::BN - 1) / T::BN);
+      const int num_kb = (Kp + T::BK - 1) / T::BK;
+      const int max_d = (T::PAIR || !g_split_k) ? 1 : kMaxSplit;
+      for (int d = 1; d <= max_d; ++d) {
+        if (!split_fits(T::kernel(), T::Cfg::kSmemBytes, EpiCfg<2>::kThreads, tiles, num_kb, d))
+          continue;
+        const int64_t waves = (tiles * d + sms - 1) / sms;
+        const int64_t cost =
+            waves * (num_kb / d) * (T::Cfg::kStageBytes / T::STAGES) +
+            (d > 1 ? kSplitFixedCost + (d - 1) * kSplitPerCtaCost : 0);
+        if (best_cost < 0 || cost < best_cost) {
+          best_cost = cost;
+          plan.variant = v;
+          plan.ksplit = d;
+        }
+      }
+      return 0;
+    });
+  }
+  return plan;
 }
 
 }  // namespace
+
+int gemm_set_split_k(int enable) {
+  const int old = g_split_k;
+  g_split_k = enable != 0;
+  return old;
+}
 
 int gemm_set_variant(int v) {
   const int old = g_forced_variant;
@@ -993,26 +1178,20 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
     return VITB200_E_ALIGNMENT;
   int* err = device_error_word();
   if (err == nullptr) return VITB200_E_INVALID_ARG;
-  int v = g_forced_variant;
-  if (v == 0 || (kVariants[v].f16 != 0) != f16) v = pick_variant(p.M, p.N, f16);
-  switch (v) {
-    case 1: return launch_variant<kKindTF32, 128, 32, 2, 4, false>(p, err, s);
-    case 2: return launch_variant<kKindTF32, 128, 16, 5, 8, false>(p, err, s);
-    case 3: return launch_variant<kKindTF32, 64, 32, 3, 4, false>(p, err, s);
-    case 4: return launch_variant<kKindTF32, 128, 32, 2, 2, false>(p, err, s);
-    case 5: return launch_variant<kKindTF32, 256, 16, 3, 8, false>(p, err, s);
-    case 6: return launch_variant<kKindTF32, 256, 32, 2, 4, true>(p, err, s);
-    case 7: return launch_variant<kKindTF32, 256, 16, 5, 8, true>(p, err, s);
-    case 8: return launch_variant<kKindTF32, 256, 16, 5, 16, true>(p, err, s);
-    case 9: return launch_variant<kKindF16, 256, 64, 2, 2, true>(p, err, s);
-    case 10: return launch_variant<kKindF16, 128, 64, 2, 2, false>(p, err, s);
-    case 11: return launch_variant<kKindF16, 64, 64, 3, 2, false>(p, err, s);
-    case 12: return launch_variant<kKindF16, 256, 32, 4, 4, true>(p, err, s);
-    case 13: return launch_variant<kKindF16SD, 256, 64, 2, 1, true>(p, err, s);
-    case 14: return launch_variant<kKindF16SD, 128, 64, 2, 1, false>(p, err, s);
-    case 15: return launch_variant<kKindF16, 256, 64, 2, 4, true>(p, err, s);
-    default: return VITB200_E_UNSUPPORTED;
-  }
+  const GemmPlan plan = plan_gemm(p.M, p.N, p.Kp, f16);
+  return with_variant(plan.variant, [&](auto t) {
+    using T = decltype(t);
+    return launch_variant<T::KIND, T::BN, T::BK, T::STAGES, T::CHUNK_KB, T::PAIR>(p, plan.ksplit,
+                                                                                 err, s);
+  });
+}
+
+int gemm_plan(int64_t M, int N, int Kp, int f16, int* variant, int* ksplit) {
+  if (M <= 0 || N <= 0 || Kp <= 0) return VITB200_E_INVALID_ARG;
+  const GemmPlan plan = plan_gemm(M, N, Kp, f16 != 0);
+  if (variant) *variant = plan.variant;
+  if (ksplit) *ksplit = plan.ksplit;
+  return 0;
 }
 
 }  // namespace vitb200

@@ -8,7 +8,7 @@ names go through ``torch.ops.vit_cuda.<op>`` (registered custom ops that
 from . import _C
 from .library import (classifier_forward, flash_attn_2, gemm_bias, layernorm_forward,
                       mlp_forward, patch_embed, pos_encoding, qkv_proj)
-from ._lib import VitB200Error, device_error
+from ._lib import VitB200Error, device_error, set_split_k
 from .model import ViTBlockCUDA, ViTCUDA
 from .pipeline import StreamedInference
 from .preprocess import preprocess
@@ -26,6 +26,7 @@ __all__ = [
     "ViTBlockCUDA",
     "VitB200Error",
     "device_error",
+    "set_split_k",
     "preprocess",
     "StreamedInference",
 ]

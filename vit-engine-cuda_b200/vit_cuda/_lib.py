@@ -67,6 +67,8 @@ _SIGNATURES = {
     "vitb200_num_sms": (c_int, []),
     "vitb200_launch_count": (ctypes.c_uint64, []),
     "vitb200_set_gemm_variant": (c_int, [c_int]),
+    "vitb200_set_split_k": (c_int, [c_int]),
+    "vitb200_gemm_plan": (c_int, [c_int64, c_int, c_int, c_int, POINTER(c_int), POINTER(c_int)]),
     "vitb200_split_tf32": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int, _P]),
     "vitb200_split_f16": (c_int, [_P, c_int64, c_int, c_int64, c_float, _P, c_int64, c_int, _P]),
     "vitb200_gemm_f16": (c_int, [_P, _P, c_float, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int,
@@ -143,3 +145,21 @@ def device_error(clear: bool = True) -> int:
     code = c_int(0)
     check(lib.vitb200_device_error(ctypes.byref(code), 1 if clear else 0), "vitb200_device_error")
     return code.value
+
+
+def set_split_k(enabled: bool) -> bool:
+    """Switches split-K of the model's small block GEMMs (on by default; a
+    batch-1 forward spreads each GEMM's K over more SMs). Off, an image's logits
+    are bitwise the same in any batch of fewer than 1024 token rows; on, they
+    agree to FP32 rounding. Affects later launches (not a captured graph).
+    Returns the previous setting; process-wide."""
+    return bool(lib.vitb200_set_split_k(1 if enabled else 0))
+
+
+def gemm_plan(M: int, K: int, N: int, f16: bool) -> tuple[int, int]:
+    """(variant, ksplit) a GEMM of this shape launched now on the current
+    device would use (vitb200_gemm_plan)."""
+    v, d = c_int(0), c_int(0)
+    check(lib.vitb200_gemm_plan(int(M), int(K), int(N), 1 if f16 else 0, ctypes.byref(v),
+                                ctypes.byref(d)), "vitb200_gemm_plan")
+    return v.value, d.value
