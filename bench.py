@@ -271,6 +271,24 @@ def cpu_oracle_rate(img_size: int, sample: int, min_seconds: float = 10.0, max_r
     return sample * reps / dt, reps, torch.get_num_threads()
 
 
+def cpu_oracle_p50_bs1(img_size: int, runs: int = 20) -> float:
+    """Median milliseconds of `runs` single-image CPU oracle forwards (fp32,
+    all host threads) after one warm-up."""
+    from oracle import vit_oracle
+    from vit_cuda.weights import synthetic_images, synthetic_state_dict
+    torch.set_num_threads(os.cpu_count() or 1)
+    state = synthetic_state_dict(seed=0, img_size=img_size)
+    img = synthetic_images(1, img_size, seed=0)
+    times = []
+    with torch.no_grad():
+        vit_oracle.vit_forward(img, state, dtype=torch.float32)
+        for _ in range(runs):
+            t0 = time.perf_counter()
+            vit_oracle.vit_forward(img, state, dtype=torch.float32)
+            times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times)
+
+
 # ----------------------------------------------------------------- arms
 def run_reference(args):
     rank, _, world = dist_env()
@@ -302,6 +320,7 @@ def run_reference(args):
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "p50_bs1_ms": {"cpu_ms": cpu_oracle_p50_bs1(img), "runs": 20},
     })
 
 
@@ -427,7 +446,8 @@ def run_ours(args):
         result["cpu_baseline"] = {
             "value": rate, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{args.cpu_sample} images x {reps} reps of the {args.config} workload "
-                      "(CPU oracle port of the reference path, fp32)"}
+                      "(CPU oracle port of the reference path, fp32)",
+            "p50_bs1_ms": cpu_oracle_p50_bs1(img)}
     if rank == 0:
         emit(result)
     if world > 1:
