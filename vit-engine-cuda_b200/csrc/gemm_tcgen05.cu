@@ -860,21 +860,12 @@ int make_planes_map(CUtensorMap* map, const void* base, int64_t rows, int Kp, in
 
 namespace {
 
-struct Variant {
-  int f16, bn, bk, stages, chunk_kb, pair;
-};
-// Index 1.. are selectable with gemm_set_variant; 0 = automatic. 1-8 take TF32
-// pairs, 9-14 FP16 splits (13, 14: two B planes with scale-input-d); a forced
-// variant of the other operand kind is ignored.
-constexpr Variant kVariants[] = {
-    {0, 0, 0, 0, 0, 0},     {0, 128, 32, 2, 4, 0}, {0, 128, 16, 5, 8, 0}, {0, 64, 32, 3, 4, 0},
-    {0, 128, 32, 2, 2, 0},  {0, 256, 16, 3, 8, 0}, {0, 256, 32, 2, 4, 1}, {0, 256, 16, 5, 8, 1},
-    {0, 256, 16, 5, 16, 1}, {1, 256, 64, 2, 2, 1}, {1, 128, 64, 2, 2, 0}, {1, 64, 64, 3, 2, 0},
-    {1, 256, 32, 4, 4, 1},  {1, 256, 64, 2, 1, 1}, {1, 128, 64, 2, 1, 0}, {1, 256, 64, 2, 4, 1},
-};
-constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+// Tile configurations 1 .. kNumVariants - 1 (with_variant below is the table);
+// 0 = automatic. 1-8 take TF32 pairs, 9-15 FP16 splits (13, 14: two B planes
+// with scale-input-d); a forced variant of the other operand kind is ignored.
+constexpr int kNumVariants = 16;
 struct GemmPlan {
-  int variant;  // index into kVariants
+  int variant;  // tile configuration (with_variant)
   int ksplit;   // K splits (clusters of ksplit CTAs per tile; 1 = none)
 };
 constexpr int kPairVariant = 6;
@@ -1035,8 +1026,8 @@ struct VariantT {
   static constexpr auto kernel() { return gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, 2>; }
 };
 
-// Calls f(VariantT<...>{}) for variant v (1 .. kNumVariants - 1); the order
-// matches kVariants.
+// The table of tile configurations: calls f(VariantT<...>{}) for variant v
+// (1 .. kNumVariants - 1).
 template <typename F>
 int with_variant(int v, F&& f) {
   switch (v) {
@@ -1077,7 +1068,9 @@ constexpr int64_t kSplitPerCtaCost = 5 * 1024;
 GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
   GemmPlan plan{0, 1};
   const int forced = g_forced_variant;
-  const bool use_forced = forced != 0 && (kVariants[forced].f16 != 0) == f16;
+  const bool use_forced =
+      forced != 0 &&
+      with_variant(forced, [](auto t) { return int{decltype(t)::KIND != kKindTF32}; }) == f16;
   if (!use_forced && M >= 1024) {
     plan.variant = f16 ? kF16PairVariant : kPairVariant;
     return plan;
@@ -1129,23 +1122,15 @@ int gemm_set_variant(int v) {
 }
 
 int gemm_prepare_device() {
-  int st = set_smem_attr<kKindTF32, 128, 32, 2, 4, false>();
-  if (!st) st = set_smem_attr<kKindTF32, 128, 16, 5, 8, false>();
-  if (!st) st = set_smem_attr<kKindTF32, 64, 32, 3, 4, false>();
-  if (!st) st = set_smem_attr<kKindTF32, 128, 32, 2, 2, false>();
-  if (!st) st = set_smem_attr<kKindTF32, 256, 16, 3, 8, false>();
-  if (!st) st = set_smem_attr<kKindTF32, 256, 32, 2, 4, true>();
-  if (!st) st = set_smem_attr<kKindTF32, 256, 16, 5, 8, true>();
-  if (!st) st = set_smem_attr<kKindTF32, 256, 16, 5, 16, true>();
-  if (!st) st = set_smem_attr<kKindF16, 256, 64, 2, 2, true>();
-  if (!st) st = set_smem_attr<kKindF16, 128, 64, 2, 2, false>();
-  if (!st) st = set_smem_attr<kKindF16, 64, 64, 3, 2, false>();
-  if (!st) st = set_smem_attr<kKindF16, 256, 32, 4, 4, true>();
-  if (!st) st = set_smem_attr<kKindF16SD, 256, 64, 2, 1, true>();
-  if (!st) st = set_smem_attr<kKindF16SD, 128, 64, 2, 1, false>();
-  if (!st) st = set_smem_attr<kKindF16, 256, 64, 2, 4, true>();
-  if (!st && encode_fn() == nullptr) st = VITB200_E_NO_TMA;
-  return st;
+  for (int v = 1; v < kNumVariants; ++v) {
+    const int st = with_variant(v, [](auto t) {
+      using T = decltype(t);
+      return set_smem_attr<T::KIND, T::BN, T::BK, T::STAGES, T::CHUNK_KB, T::PAIR>();
+    });
+    if (st) return st;
+  }
+  if (encode_fn() == nullptr) return VITB200_E_NO_TMA;
+  return 0;
 }
 
 int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
