@@ -69,6 +69,14 @@ int vitb200_init(void);
  * when no kernel reported an error. */
 int vitb200_device_error(int* code, int clear);
 
+/* Failure-reporting check: launches a kernel whose bounded wait is never
+ * satisfied (kind 0: the GEMM / attention pipeline wait, which reports code
+ * 1; kind 1: the split-K leader's cluster-scope wait, code 7). After the wait
+ * limit (1 s) it records the code in the device error word and returns; the
+ * context stays usable. No counterpart in the reference (its kernels have no
+ * waits). */
+int vitb200_check_wait_timeout(int kind, void* stream);
+
 /* Number of streaming multiprocessors the launch heuristics use. */
 int vitb200_num_sms(void);
 

@@ -175,6 +175,13 @@ int vitb200_set_gemm_variant(int variant) { return gemm_set_variant(variant); }
 
 int vitb200_set_split_k(int enable) { return gemm_set_split_k(enable); }
 
+int vitb200_check_wait_timeout(int kind, void* stream) {
+  VITB200_GUARD_BEGIN
+  if (int st = check_ready()) return st;
+  return wait_timeout_launch(kind, as_stream(stream));
+  VITB200_GUARD_END
+}
+
 int vitb200_gemm_plan(int64_t M, int K, int N, int f16, int* variant, int* ksplit) {
   VITB200_GUARD_BEGIN
   if (M <= 0 || K <= 0 || N <= 0) return VITB200_E_INVALID_ARG;

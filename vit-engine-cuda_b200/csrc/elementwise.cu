@@ -505,4 +505,33 @@ int gemm_k0_launch(const GemmProblem& p, cudaStream_t s) {
   return cuda_status(cudaGetLastError());
 }
 
+// ----------------------------------------------------------- diagnostics
+// A wait that nothing completes: thread 0 waits on a fresh mbarrier (phase 0
+// never completes) with the same bounded helpers the GEMM and attention
+// kernels use. After the time limit it records its code in the device error
+// word and returns; nothing faults and the context stays usable.
+__global__ void wait_timeout_kernel(int* err, int kind) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (kind == 0) {
+      (void)mbar_wait(&bar, 0, err, kErrWaitFull);
+    } else {
+      (void)mbar_wait_acq_cluster(&bar, 0, err, kErrWaitSplit);
+    }
+  }
+}
+
+int wait_timeout_launch(int kind, cudaStream_t s) {
+  if (kind != 0 && kind != 1) return VITB200_E_INVALID_ARG;
+  int* err = device_error_word();
+  if (err == nullptr) return VITB200_E_INVALID_ARG;
+  if (int st = launch_kernel(wait_timeout_kernel, dim3(1), dim3(32), 0, s, 1, err, kind)) return st;
+  return cuda_status(cudaGetLastError());
+}
+
 }  // namespace vitb200

@@ -89,6 +89,9 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t stream);
 int gemm_prepare_device();
 // Forces one tile configuration (0 = automatic choice); returns the old value.
 int gemm_set_variant(int v);
+// Launches a kernel whose bounded wait never completes (kind 0: a pipeline
+// wait, error code 1; 1: the split-K leader's cluster-scope wait, code 7).
+int wait_timeout_launch(int kind, cudaStream_t s);
 // Switches split-K of later small single-CTA launches on / off; returns the
 // old setting.
 int gemm_set_split_k(int enable);

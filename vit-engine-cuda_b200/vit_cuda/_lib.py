@@ -68,6 +68,7 @@ _SIGNATURES = {
     "vitb200_launch_count": (ctypes.c_uint64, []),
     "vitb200_set_gemm_variant": (c_int, [c_int]),
     "vitb200_set_split_k": (c_int, [c_int]),
+    "vitb200_check_wait_timeout": (c_int, [c_int, _P]),
     "vitb200_gemm_plan": (c_int, [c_int64, c_int, c_int, c_int, POINTER(c_int), POINTER(c_int)]),
     "vitb200_split_tf32": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int, _P]),
     "vitb200_split_f16": (c_int, [_P, c_int64, c_int, c_int64, c_float, _P, c_int64, c_int, _P]),
