@@ -422,30 +422,58 @@ __global__ void __launch_bounds__(kThreadsF, 1)
         // with s_scale = scale * log2(e) (and the operand scales) and m' the
         // running maximum in the same units; one FMA rounds each argument.
         const int nvalid = a.T - j * kKV;
-        if (nvalid < kKV) {  // the ragged last tile (uniform across the warpgroup)
-#pragma unroll
-          for (int c = 0; c < kKV; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
-        }
-        float cmax = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < kKV; ++c) cmax = fmaxf(cmax, s[c]);
-        const float m_new = fmaxf(m_run, cmax * a.s_scale);
-        const float alpha = exp2_nonpos(m_run - m_new);
-        float psum = 0.f;
-#pragma unroll
-        for (int c = 0; c < kKV; ++c) {
-          s[c] = exp2_nonpos(fmaf(s[c], a.s_scale, -m_new));
-          psum += s[c];
-        }
-        l_run = l_run * alpha + psum;
+        float m_new, alpha;
         // P's FP16 split into this set's S columns: hi words, then lo words.
         float ph[32], pl[32];
+        if (nvalid <= 16) {
+          // A ragged last tile of at most 16 keys (T = 197: 5, T = 577: 1;
+          // uniform across the warpgroup): the arithmetic covers 16 keys and
+          // the other 48 P entries are zero.
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          uint32_t hw, lw;
-          h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
-          ph[c] = __uint_as_float(hw);
-          pl[c] = __uint_as_float(lw);
+          for (int c = 0; c < 16; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) cmax = fmaxf(cmax, s[c]);
+          m_new = fmaxf(m_run, cmax * a.s_scale);
+          alpha = exp2_nonpos(m_run - m_new);
+          float psum = 0.f;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            s[c] = exp2_nonpos(fmaf(s[c], a.s_scale, -m_new));
+            psum += s[c];
+          }
+          l_run = l_run * alpha + psum;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            uint32_t hw = 0, lw = 0;
+            if (c < 8) h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
+            ph[c] = __uint_as_float(hw);
+            pl[c] = __uint_as_float(lw);
+          }
+        } else {
+          if (nvalid < kKV) {  // a ragged last tile (uniform across the warpgroup)
+#pragma unroll
+            for (int c = 0; c < kKV; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
+          }
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < kKV; ++c) cmax = fmaxf(cmax, s[c]);
+          m_new = fmaxf(m_run, cmax * a.s_scale);
+          alpha = exp2_nonpos(m_run - m_new);
+          float psum = 0.f;
+#pragma unroll
+          for (int c = 0; c < kKV; ++c) {
+            s[c] = exp2_nonpos(fmaf(s[c], a.s_scale, -m_new));
+            psum += s[c];
+          }
+          l_run = l_run * alpha + psum;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            uint32_t hw, lw;
+            h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
+            ph[c] = __uint_as_float(hw);
+            pl[c] = __uint_as_float(lw);
+          }
         }
         __syncwarp();
         tmem_st_32x32b_x32(scol, ph);
