@@ -78,8 +78,9 @@ def parse_args():
     ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-p50", action="store_true")
-    ap.add_argument("--mode", choices=["full", "roofline"], default="full",
-                    help="roofline: time only the dominant GEMM launch (for ncu captures)")
+    ap.add_argument("--mode", choices=["full", "roofline", "peaks"], default="full",
+                    help="roofline: time only the dominant GEMM launch (for ncu captures); "
+                         "peaks: measure cuBLAS TF32 / bf16 / fp16 GEMM throughput")
     ap.add_argument("--batch", type=int, default=None, help="override images per GPU")
     ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS) + ["attention"], default="fc1",
                     help="roofline mode: which block GEMM (or the attention) to time")
@@ -562,8 +563,61 @@ def run_roofline_only(args):
           "kernel_ms": ms, "f16_pipe_tflops": 3 * 2.0 * M * N * K / (ms * 1e-3) / 1e12})
 
 
+def run_peaks():
+    """Dense tensor throughput of cuBLAS (torch.matmul) at 8192^3 on this GPU:
+    TF32 (fp32 inputs with TF32 allowed), bf16 and fp16; burst = best of 10
+    launches, sustained = back-to-back launches for about 3 s (power capped).
+    TF32 is the north star's formulation (TF32x3 costs three TF32 products per
+    multiply); the repository's kernels run FP16 products."""
+    dev = torch.device("cuda", 0)
+    n = 8192
+    flops = 2.0 * n ** 3
+    out = {"mode": "peaks", "shape": f"{n}^3"}
+
+    def measure(dtype, tf32, seconds):
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+        a = torch.randn(n, n, device=dev).to(dtype)
+        b = torch.randn(n, n, device=dev).to(dtype)
+        for _ in range(3):
+            a @ b
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            a @ b
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        burst = flops / (best * 1e-3) / 1e12
+        reps = max(1, int(seconds / (best * 1e-3)))
+        clocks = ClockSampler(0)
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            a @ b
+        e1.record()
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        sustained = flops * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+        torch.backends.cuda.matmul.allow_tf32 = False
+        return burst, sustained, clk
+
+    for name, dtype, tf32 in (("tf32", torch.float32, True), ("bf16", torch.bfloat16, False),
+                              ("fp16", torch.float16, False)):
+        burst, sustained, clk = measure(dtype, tf32, 3.0)
+        out[f"{name}_tflops"] = burst
+        out[f"{name}_tflops_sustained"] = sustained
+        out[f"{name}_clocks_sustained"] = clk
+    emit(out)
+
+
 def main():
     args = parse_args()
+    if args.mode == "peaks":
+        run_peaks()
+        return
     if args.mode == "roofline":
         run_roofline_only(args)
         return
