@@ -82,8 +82,10 @@ def parse_args():
                     help="roofline: time only the dominant GEMM launch (for ncu captures); "
                          "peaks: measure cuBLAS TF32 / bf16 / fp16 GEMM throughput")
     ap.add_argument("--batch", type=int, default=None, help="override images per GPU")
-    ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS) + ["attention"], default="fc1",
-                    help="roofline mode: which block GEMM (or the attention) to time")
+    ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS) + ["attention", "attention_tf32",
+                                                                 "patch"], default="fc1",
+                    help="roofline mode: which block GEMM (FP16 splits), the FP16-split "
+                         "attention, or the per-op TF32x3 attention / patch GEMM to time")
     return ap.parse_args()
 
 
@@ -540,6 +542,36 @@ def attention_roofline(dev, B: int, T: int, reps: int = 10):
     return e0.elapsed_time(e1) / reps
 
 
+def per_op_roofline(dev, B: int, T: int, kernel: str, reps: int = 10):
+    """Times a per-op TF32x3 entry point as a user calls it (its operand splits
+    included): vit_cuda._C.flash_attn_2 on [B, T, 768] q, k, v, or
+    vit_cuda._C.gemm_bias for the patch projection (768 -> 768 over B*T rows);
+    returns ms per call."""
+    from vit_cuda import _C
+    if kernel == "attention_tf32":
+        q, k, v = (torch.randn(B, T, 768, device=dev) for _ in range(3))
+
+        def launch():
+            _C.flash_attn_2(q, k, v, 0.125)
+    else:
+        x = torch.randn(B * T, 768, device=dev)
+        w = torch.randn(768, 768, device=dev) * 0.02
+        b = torch.randn(768, device=dev) * 0.02
+
+        def launch():
+            _C.gemm_bias(x, w, b)
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
 def run_roofline_only(args):
     """The dominant kernel alone (fc1 shape for `batch` images), a small case
     for profilers; prints one JSON line with its CUDA-event time."""
@@ -551,6 +583,14 @@ def run_roofline_only(args):
         batch = args.batch
     T = (img // 16) ** 2 + 1
     M = batch * T
+    if args.kernel in ("attention_tf32", "patch"):
+        ms = per_op_roofline(dev, batch, T, args.kernel, reps=max(1, args.steps))
+        flop = (4.0 * batch * 12 * T * T * 64 if args.kernel == "attention_tf32"
+                else 2.0 * M * 768 * 768)
+        emit({"mode": "roofline", "kernel": f"per-op TF32x3 {args.kernel} (splits included)",
+              "B": batch, "T": T, "M": M, "call_ms": ms,
+              "algorithmic_tflops": flop / (ms * 1e-3) / 1e12})
+        return
     if args.kernel == "attention":
         ms = attention_roofline(dev, batch, T, reps=max(1, args.steps))
         emit({"mode": "roofline", "kernel": "attention f16 (splits + attention_f16_kernel)",
