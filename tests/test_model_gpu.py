@@ -233,3 +233,18 @@ def test_streamed_inference_matches_eager(cuda):
     with torch.no_grad():
         for x, o in zip(batches, outs):
             torch.testing.assert_close(o, model(x.to(cuda)).cpu(), atol=0, rtol=0)
+
+
+def test_fused_head_matches_gemm_head(case224, cuda):
+    """Up to 16 images the final LayerNorm and the head run as one CUDA-core
+    kernel; above, as LayerNorm + head GEMM. Batches of 16 and 17 share their
+    block arithmetic (both take the CTA-pair tiles), so their logits differ by
+    the head's rounding only; both match the oracle."""
+    state, _, _, _, model = case224
+    x = synthetic_images(17, 224, seed=11)
+    with torch.no_grad():
+        gemm_head = model(x.to(cuda)).double().cpu()
+        fused_head = model(x[:16].to(cuda)).double().cpu()
+    assert (gemm_head[:16] - fused_head).abs().max().item() <= 2e-5
+    ref = orc.vit_forward(x[:2], state)
+    assert (fused_head[:2] - ref).abs().max().item() <= LOGITS_ATOL

@@ -848,13 +848,20 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
 }
 
 // Final LayerNorm on the CLS rows only (the head reads token 0 alone), then
-// the head GEMM. features / logits may each be null.
+// the head GEMM; up to kFusedHeadMaxBatch images one fused kernel does both
+// (CUDA-core dot products: the GEMM launch there is all latency). features /
+// logits may each be null.
+constexpr int kFusedHeadMaxBatch = 16;
+
 int vit_head(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, const float* x,
              float* logits, float* features, int batch, cudaStream_t s) {
   const int D = p->embed_dim;
   const int64_t cls_stride = static_cast<int64_t>(d.T) * D;
   const bool want_logits = logits != nullptr && p->num_classes > 0;
   if (!features && !want_logits) return 0;
+  if (want_logits && batch <= kFusedHeadMaxBatch && D == 768 && cls_stride % 4 == 0)
+    return cls_head_launch(x, cls_stride, p->norm_w, p->norm_b, p->ln_eps, p->head_w_pair,
+                           p->head_b, p->num_classes, D, batch, logits, features, s);
   if (int st = layernorm_launch(x, cls_stride, p->norm_w, p->norm_b, features, D,
                                 want_logits ? b.cls_pair : nullptr, D,
                                 static_cast<int64_t>(batch) * D, batch, D, p->ln_eps, s))

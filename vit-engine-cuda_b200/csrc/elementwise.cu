@@ -138,6 +138,33 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // E = 768: the row lives in registers (6 float4 per lane), read once.
+// LayerNorm of one 768-wide row by one warp: lane holds float4 columns
+// lane + 32 i (i < 6) of x in v and gets the normalised values in o.
+__device__ __forceinline__ void layernorm768_row(const float4 (&v)[6], const float4 (&g)[6],
+                                                 const float4 (&b)[6], float eps,
+                                                 float4 (&o)[6]) {
+  constexpr int E = 768;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  const float mean = warp_sum(s) / static_cast<float>(E);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const float a0 = v[i].x - mean, a1 = v[i].y - mean, a2 = v[i].z - mean, a3 = v[i].w - mean;
+    q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+  }
+  const float var = warp_sum(q) / static_cast<float>(E);
+  const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    o[i].x = (v[i].x - mean) * rstd * g[i].x + b[i].x;
+    o[i].y = (v[i].y - mean) * rstd * g[i].y + b[i].y;
+    o[i].z = (v[i].z - mean) * rstd * g[i].z + b[i].z;
+    o[i].w = (v[i].w - mean) * rstd * g[i].w + b[i].w;
+  }
+}
+
 __global__ void __launch_bounds__(256) layernorm768_kernel(
     const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma,
     const float* __restrict__ beta, float* __restrict__ y, int64_t ldy, float* __restrict__ yp,
@@ -158,29 +185,13 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
   }
   for (int64_t r = warp_global; r < rows; r += nwarps) {
     const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
-    float4 v[V];
-    float s = 0.f;
+    float4 v[V], ov[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+    layernorm768_row(v, g, b, eps, ov);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      v[i] = __ldcs(xr + lane + 32 * i);
-      s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    }
-    const float mean = warp_sum(s) / static_cast<float>(E);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const float a0 = v[i].x - mean, a1 = v[i].y - mean, a2 = v[i].z - mean, a3 = v[i].w - mean;
-      q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
-    }
-    const float var = warp_sum(q) / static_cast<float>(E);
-    const float rstd = 1.0f / sqrtf(var + eps);
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      float4 o;
-      o.x = (v[i].x - mean) * rstd * g[i].x + b[i].x;
-      o.y = (v[i].y - mean) * rstd * g[i].y + b[i].y;
-      o.z = (v[i].z - mean) * rstd * g[i].z + b[i].z;
-      o.w = (v[i].w - mean) * rstd * g[i].w + b[i].w;
+      const float4 o = ov[i];
       const int col = (lane + 32 * i) * 4;
       if (y) *reinterpret_cast<float4*>(y + r * ldy + col) = o;
       if (yp) {
@@ -204,6 +215,91 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
       }
     }
   }
+}
+
+// Final LayerNorm of each image's CLS row fused with the classifier head, for
+// small batches (the head GEMM there is all launch latency): blockIdx.y is the
+// image; warp 0 normalises its CLS row into shared memory with the LayerNorm
+// kernel's arithmetic (features of block 0 written out), then each warp takes
+// kHeadClassesPerWarp classes: FP32 dot products against the head weight's
+// TF32 pair, y . hi + y . lo (hi + lo is w to 2^-22), plus the bias.
+constexpr int kHeadClassesPerWarp = 4;
+constexpr int kHeadClassesPerBlock = 8 * kHeadClassesPerWarp;
+
+__global__ void __launch_bounds__(256) cls_head768_kernel(
+    const float* __restrict__ x, int64_t cls_stride, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float eps, const float* __restrict__ w_pair,
+    const float* __restrict__ bias, int C, float* __restrict__ logits,
+    float* __restrict__ features) {
+  griddep_wait();
+  griddep_launch_dependents();
+  constexpr int E = 768;
+  constexpr int V = E / 128;
+  __shared__ __align__(16) float4 ys[E / 4];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t img = blockIdx.y;
+  if (warp == 0) {
+    const float4* xr = reinterpret_cast<const float4*>(x + img * cls_stride);
+    float4 v[V], g[V], b[V], o[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      v[i] = __ldg(xr + lane + 32 * i);
+      g[i] = __ldg(reinterpret_cast<const float4*>(gamma) + lane + 32 * i);
+      b[i] = __ldg(reinterpret_cast<const float4*>(beta) + lane + 32 * i);
+    }
+    layernorm768_row(v, g, b, eps, o);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      ys[lane + 32 * i] = o[i];
+      if (features && blockIdx.x == 0)
+        reinterpret_cast<float4*>(features + img * E)[lane + 32 * i] = o[i];
+    }
+  }
+  __syncthreads();
+  float4 y[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) y[i] = ys[lane + 32 * i];
+  const float4* hi_plane = reinterpret_cast<const float4*>(w_pair);
+  const float4* lo_plane = reinterpret_cast<const float4*>(w_pair + static_cast<int64_t>(C) * E);
+#pragma unroll 1
+  for (int k = 0; k < kHeadClassesPerWarp; ++k) {
+    const int c = blockIdx.x * kHeadClassesPerBlock + warp * kHeadClassesPerWarp + k;
+    if (c >= C) break;  // uniform across the warp
+    const float4* hr = hi_plane + static_cast<int64_t>(c) * (E / 4);
+    const float4* lr = lo_plane + static_cast<int64_t>(c) * (E / 4);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 h = __ldg(hr + lane + 32 * i);
+      const float4 l = __ldg(lr + lane + 32 * i);
+      acc = fmaf(y[i].x, h.x, acc);
+      acc = fmaf(y[i].x, l.x, acc);
+      acc = fmaf(y[i].y, h.y, acc);
+      acc = fmaf(y[i].y, l.y, acc);
+      acc = fmaf(y[i].z, h.z, acc);
+      acc = fmaf(y[i].z, l.z, acc);
+      acc = fmaf(y[i].w, h.w, acc);
+      acc = fmaf(y[i].w, l.w, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[img * C + c] = acc + __ldg(bias + c);
+  }
+}
+
+int cls_head_launch(const float* x, int64_t cls_stride, const float* gamma, const float* beta,
+                    float eps, const float* w_pair, const float* bias, int C, int E, int batch,
+                    float* logits, float* features, cudaStream_t s) {
+  auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (E != 768 || batch <= 0 || C <= 0 || !x || !gamma || !beta || !w_pair || !bias || !logits ||
+      cls_stride % 4 != 0 || !al(x) || !al(gamma) || !al(beta) || !al(w_pair) ||
+      (features && !al(features)))
+    return VITB200_E_INVALID_ARG;
+  const dim3 grid((C + kHeadClassesPerBlock - 1) / kHeadClassesPerBlock, batch);
+  if (int st = launch_kernel(cls_head768_kernel, grid, dim3(256), 0, s, 1, x, cls_stride, gamma,
+                             beta, eps, w_pair, bias, C, logits, features))
+    return st;
+  return cuda_status(cudaGetLastError());
 }
 
 // Any E: three passes over the row (the re-reads hit L1/L2).

@@ -116,6 +116,12 @@ int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const floa
                      float* y, int64_t ldy, float* y_pair, int64_t pair_ld, int64_t pair_plane,
                      int64_t rows, int E, float eps, cudaStream_t s, uint16_t* y_h16 = nullptr,
                      int64_t h16_ld = 0, int64_t h16_plane = 0);
+// Final LayerNorm of each image's CLS row (rows x + b * cls_stride, E = 768)
+// fused with the head (TF32 pair [2][C][768] + bias) for small batches:
+// logits [batch][C] and optionally the normalised features [batch][768].
+int cls_head_launch(const float* x, int64_t cls_stride, const float* gamma, const float* beta,
+                    float eps, const float* w_pair, const float* bias, int C, int E, int batch,
+                    float* logits, float* features, cudaStream_t s);
 int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair, cudaStream_t s);
 int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const float* patches,
                    float* out, int B, int P, int E, cudaStream_t s);
