@@ -180,29 +180,29 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
   const bool row_ok = m < a.M;
   const bool full = (n0 + 32 <= N);
 
-  if constexpr (F16) {
-    // Undo the operand scales: exact, a power of two.
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = v[j] * a.acc_scale;
-  }
-
+  // Undo the operand scales (FP16 kinds; a power of two, so the product is
+  // exact) and add the bias: one rounding, as acc * scale + bias would give.
+  const float sc = F16 ? a.acc_scale : 1.f;
   if (e.bias != nullptr) {
     if (full && a.vec_bias) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
         const float4 b4 = __ldg(reinterpret_cast<const float4*>(e.bias + n0 + j));
-        v[j] = v[j] + b4.x;
-        v[j + 1] = v[j + 1] + b4.y;
-        v[j + 2] = v[j + 2] + b4.z;
-        v[j + 3] = v[j + 3] + b4.w;
+        v[j] = fmaf(v[j], sc, b4.x);
+        v[j + 1] = fmaf(v[j + 1], sc, b4.y);
+        v[j + 2] = fmaf(v[j + 2], sc, b4.z);
+        v[j + 3] = fmaf(v[j + 3], sc, b4.w);
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int n = n0 + j;
-        v[j] = v[j] + ((n < N) ? __ldg(e.bias + n) : 0.f);
+        v[j] = fmaf(v[j], sc, (n < N) ? __ldg(e.bias + n) : 0.f);
       }
     }
+  } else if constexpr (F16) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = v[j] * sc;
   }
   if (e.gelu) {
 #pragma unroll
