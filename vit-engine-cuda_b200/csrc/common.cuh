@@ -107,9 +107,11 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
          (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
 }
 
-// Exact (erf) GELU, the activation of timm's ViT MLP.
+// Exact (erf) GELU, the activation of timm's ViT MLP: h + h * erf(x / sqrt 2)
+// with h = x / 2 (exact), one rounding.
 __device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+  const float h = 0.5f * x;
+  return fmaf(h, erff(x * 0.70710678118654752440f), h);
 }
 
 // ---- shared memory / mbarrier -----------------------------------------
