@@ -78,7 +78,8 @@ def test_gemm_f16_bands(vlib, cuda, shape, h16):
         assert bands_intact(hbuf, 12345)
 
 
-@pytest.mark.parametrize("B,T", [(2, 197), (1, 577), (3, 50), (1, 1), (2, 65)])
+@pytest.mark.parametrize("B,T", [(2, 197), (1, 577), (3, 50), (1, 1), (2, 65), (13, 197),
+                                 (7, 577)])
 def test_attention_f16_bands(vlib, cuda, B, T):
     torch.manual_seed(2)
     E = 768

@@ -67,13 +67,13 @@ def compile_one(src: str) -> tuple[str, str]:
 
 
 # Kernels that move registers between warpgroups with setmaxnreg, and the
-# per-thread register count their split assumes. csrc/attention_f16.cu: 384
-# threads launched at 168. csrc/gemm_tcgen05.cu: the last template argument
+# per-thread register count their split assumes. csrc/attention_f16.cu and
+# csrc/attention_f16_tile.cu: 384 threads launched at 168. csrc/gemm_tcgen05.cu: the last template argument
 # (EPI, the number of epilogue warpgroups) sets it: 2 -> 384 threads at 168,
 # 4 -> 640 threads at 96 (EpiCfg there). A kernel compiled to any other count
 # could make setmaxnreg.inc wait forever.
 def expected_registers(mangled: str) -> int | None:
-    if "attention_f16_kernel" in mangled:
+    if "attention_f16_kernel" in mangled or "attention_f16_tile_kernel" in mangled:
         return 168
     m = re.search(r"gemm_tf32x3_kernelI(.*?)EEv", mangled)
     if m:

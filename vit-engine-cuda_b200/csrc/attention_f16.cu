@@ -39,6 +39,7 @@
 
 #include <algorithm>
 
+#include "attention_f16.cuh"
 #include "common.cuh"
 #include "engine.h"
 #include "vitb200.h"
@@ -80,55 +81,7 @@ static_assert(128 * kCtrlRegsF + 256 * kSoftRegsF == 384 * 168, "register split"
 static_assert(kSmemF <= 227 * 1024, "shared memory");
 }  // namespace
 
-struct AttnF16Args {
-  int T;
-  int n_kv;       // key tiles per item
-  int heads;
-  int nq;         // query tiles per image
-  int qpairs;     // ceil(nq / 2)
-  int n_items;    // images * heads * qpairs
-  float s_scale;  // log2(e) * softmax scale / (q_scale * k_scale): S -> log2 units
-  float o_scale;  // 1 / v_scale
-  float* o;       // fp32 O [M][ldo] or null
-  int64_t ldo;
-  float* o_pair;  // TF32 pair of O (planes hi | lo) or null
-  int64_t pld;
-  int64_t pplane;
-  uint16_t* o_h16;  // FP16 split of O (planes hi | lo*2^11) or null
-  int64_t hld;
-  int64_t hplane;
-  int* err;
-};
-
 namespace {
-
-__device__ __forceinline__ bool f16_warp_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                              int lane) {
-  int ok = 1;
-  if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  return ok != 0;
-}
-
-// 2^x for x <= 0 (the hardware approximation, relative error about 2^-22,
-// below the FP16 split's own; results under 2^-126 flush to zero, where a
-// probability no longer matters against a row maximum of 1).
-__device__ __forceinline__ float exp2_nonpos(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ void f16_drain_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const uint32_t addr = smem_addr(bar);
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(addr, parity)) {
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-      report_error(err, kErrDrain);
-      return;
-    }
-  }
-}
 
 struct Item {
   int b, h, qt0, nqt;
@@ -566,8 +519,10 @@ __global__ void __launch_bounds__(kThreadsF, 1)
 }
 
 int attention_f16_prepare_device() {
-  return cuda_status(cudaFuncSetAttribute(attention_f16_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemF));
+  if (int st = cuda_status(cudaFuncSetAttribute(
+          attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemF)))
+    return st;
+  return attention_f16_tile_prepare_device();
 }
 
 int attention_f16_launch(const uint16_t* q16, const uint16_t* k16, int64_t ld, const uint16_t* vt16,
@@ -621,6 +576,12 @@ int attention_f16_launch(const uint16_t* q16, const uint16_t* k16, int64_t ld, c
   a.hplane = h16_plane;
   a.err = device_error_word();
   if (a.err == nullptr) return VITB200_E_INVALID_ARG;
+  // Small batches (two-tile items filling under half the SMs, e.g. batch 1:
+  // 12 items): one query tile per item instead (attention_f16_tile.cu).
+  if (2 * items < device_num_sms()) {
+    a.n_items = static_cast<int>(static_cast<int64_t>(B) * heads * a.nq);
+    return attention_f16_tile_launch(tq, tk, tvt, a, s);
+  }
   const int grid = static_cast<int>(std::min<int64_t>(items, device_num_sms()));
   if (int st = launch_kernel(attention_f16_kernel, dim3(grid), dim3(kThreadsF), kSmemF, s, 1, tq, tk,
                              tvt, a))
