@@ -219,12 +219,11 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
 
 // Final LayerNorm of each image's CLS row fused with the classifier head, for
 // small batches (the head GEMM there is all launch latency): blockIdx.y is the
-// image; warp 0 normalises its CLS row into shared memory with the LayerNorm
-// kernel's arithmetic (features of block 0 written out), then each warp takes
-// kHeadClassesPerWarp classes: FP32 dot products against the head weight's
-// TF32 pair, y . hi + y . lo (hi + lo is w to 2^-22), plus the bias.
-constexpr int kHeadClassesPerWarp = 4;
-constexpr int kHeadClassesPerBlock = 8 * kHeadClassesPerWarp;
+// image; every warp loads its class's head row (the TF32 pair, hi + lo is w to
+// 2^-22) while warp 0 normalises the CLS row into shared memory with the
+// LayerNorm kernel's arithmetic (features of block 0 written out); then each
+// warp takes the FP32 dot product y . hi + y . lo plus the bias.
+constexpr int kHeadClassesPerBlock = 8;  // one per warp
 
 __global__ void __launch_bounds__(256) cls_head768_kernel(
     const float* __restrict__ x, int64_t cls_stride, const float* __restrict__ gamma,
@@ -239,6 +238,18 @@ __global__ void __launch_bounds__(256) cls_head768_kernel(
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t img = blockIdx.y;
+  const int c = blockIdx.x * kHeadClassesPerBlock + warp;
+  float4 h[V], l[V];
+  if (c < C) {
+    const float4* hr = reinterpret_cast<const float4*>(w_pair) + static_cast<int64_t>(c) * (E / 4);
+    const float4* lr = reinterpret_cast<const float4*>(w_pair + static_cast<int64_t>(C) * E) +
+                       static_cast<int64_t>(c) * (E / 4);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      h[i] = __ldg(hr + lane + 32 * i);
+      l[i] = __ldg(lr + lane + 32 * i);
+    }
+  }
   if (warp == 0) {
     const float4* xr = reinterpret_cast<const float4*>(x + img * cls_stride);
     float4 v[V], g[V], b[V], o[V];
@@ -257,34 +268,22 @@ __global__ void __launch_bounds__(256) cls_head768_kernel(
     }
   }
   __syncthreads();
-  float4 y[V];
+  if (c >= C) return;  // uniform across the warp
+  float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < V; ++i) y[i] = ys[lane + 32 * i];
-  const float4* hi_plane = reinterpret_cast<const float4*>(w_pair);
-  const float4* lo_plane = reinterpret_cast<const float4*>(w_pair + static_cast<int64_t>(C) * E);
-#pragma unroll 1
-  for (int k = 0; k < kHeadClassesPerWarp; ++k) {
-    const int c = blockIdx.x * kHeadClassesPerBlock + warp * kHeadClassesPerWarp + k;
-    if (c >= C) break;  // uniform across the warp
-    const float4* hr = hi_plane + static_cast<int64_t>(c) * (E / 4);
-    const float4* lr = lo_plane + static_cast<int64_t>(c) * (E / 4);
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const float4 h = __ldg(hr + lane + 32 * i);
-      const float4 l = __ldg(lr + lane + 32 * i);
-      acc = fmaf(y[i].x, h.x, acc);
-      acc = fmaf(y[i].x, l.x, acc);
-      acc = fmaf(y[i].y, h.y, acc);
-      acc = fmaf(y[i].y, l.y, acc);
-      acc = fmaf(y[i].z, h.z, acc);
-      acc = fmaf(y[i].z, l.z, acc);
-      acc = fmaf(y[i].w, h.w, acc);
-      acc = fmaf(y[i].w, l.w, acc);
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) logits[img * C + c] = acc + __ldg(bias + c);
+  for (int i = 0; i < V; ++i) {
+    const float4 y = ys[lane + 32 * i];
+    acc = fmaf(y.x, h[i].x, acc);
+    acc = fmaf(y.x, l[i].x, acc);
+    acc = fmaf(y.y, h[i].y, acc);
+    acc = fmaf(y.y, l[i].y, acc);
+    acc = fmaf(y.z, h[i].z, acc);
+    acc = fmaf(y.z, l[i].z, acc);
+    acc = fmaf(y.w, h[i].w, acc);
+    acc = fmaf(y.w, l[i].w, acc);
   }
+  acc = warp_sum(acc);
+  if (lane == 0) logits[img * C + c] = acc + __ldg(bias + c);
 }
 
 int cls_head_launch(const float* x, int64_t cls_stride, const float* gamma, const float* beta,
