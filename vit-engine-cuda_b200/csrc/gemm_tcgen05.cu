@@ -30,6 +30,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -870,13 +871,15 @@ struct GemmPlan {
 };
 constexpr int kPairVariant = 6;
 constexpr int kF16PairVariant = 15;
-int g_forced_variant = 0;
+// Process-wide switches and per-device caches; atomic, since host threads
+// (one per GPU, say) may launch concurrently.
+std::atomic<int> g_forced_variant{0};
 // Split-K of small single-CTA launches (on unless switched off).
-int g_split_k = 1;
+std::atomic<int> g_split_k{1};
 
 // Cluster-of-two slots that fit on the device at once, per device (0 = not
 // queried yet).
-int g_pair_slots[64] = {};
+std::atomic<int> g_pair_slots[64] = {};
 
 constexpr int kMaxSplit = 8;  // portable cluster size
 
@@ -884,14 +887,14 @@ constexpr int kMaxSplit = 8;  // portable cluster size
 // per device and d; 0 when the query fails).
 template <typename Kernel>
 int split_cluster_slots(Kernel kernel, int smem, int threads, int d) {
-  static int cache[64][kMaxSplit + 1] = {};
+  static std::atomic<int> cache[64][kMaxSplit + 1] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     (void)cudaGetLastError();
     return 0;
   }
-  int& slot = cache[dev][d];
-  if (slot == 0) {
+  std::atomic<int>& slot = cache[dev][d];
+  if (slot.load(std::memory_order_relaxed) == 0) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -908,9 +911,10 @@ int split_cluster_slots(Kernel kernel, int smem, int threads, int d) {
       (void)cudaGetLastError();
       n = -1;
     }
-    slot = n;
+    slot.store(n, std::memory_order_relaxed);
   }
-  return slot > 0 ? slot : 0;
+  const int v = slot.load(std::memory_order_relaxed);
+  return v > 0 ? v : 0;
 }
 
 // Whether a single-CTA launch of `tiles` output tiles over num_kb K blocks can
@@ -981,7 +985,7 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int slots = (dev >= 0 && dev < 64) ? g_pair_slots[dev] : 0;
+    int slots = (dev >= 0 && dev < 64) ? g_pair_slots[dev].load(std::memory_order_relaxed) : 0;
     if (slots <= 0) {
       cfg.gridDim = dim3(2 * static_cast<unsigned>(device_num_sms() / 2));
       if (cudaOccupancyMaxActiveClusters(&slots, gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>,
@@ -990,7 +994,7 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
         (void)cudaGetLastError();
         slots = device_num_sms() / 2;
       }
-      if (dev >= 0 && dev < 64) g_pair_slots[dev] = slots;
+      if (dev >= 0 && dev < 64) g_pair_slots[dev].store(slots, std::memory_order_relaxed);
     }
     const dim3 grid(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
     st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
@@ -1110,14 +1114,13 @@ GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
 }  // namespace
 
 int gemm_set_split_k(int enable) {
-  const int old = g_split_k;
-  g_split_k = enable != 0;
+  const int old = g_split_k.exchange(enable != 0 ? 1 : 0);
   return old;
 }
 
 int gemm_set_variant(int v) {
-  const int old = g_forced_variant;
-  if (v >= 0 && v < kNumVariants) g_forced_variant = v;
+  const int old = g_forced_variant.load();
+  if (v >= 0 && v < kNumVariants) g_forced_variant.store(v);
   return old;
 }
 
