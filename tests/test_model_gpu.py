@@ -248,3 +248,38 @@ def test_fused_head_matches_gemm_head(case224, cuda):
     assert (gemm_head[:16] - fused_head).abs().max().item() <= 2e-5
     ref = orc.vit_forward(x[:2], state)
     assert (fused_head[:2] - ref).abs().max().item() <= LOGITS_ATOL
+
+
+def test_concurrent_host_threads_match_serial(case224, cuda):
+    """Two host threads call the forward at once, each on its own stream (ctypes
+    releases the GIL, so the library is entered concurrently): results equal
+    the serial ones bitwise."""
+    import threading
+    _, _, _, _, model = case224
+    xs = [synthetic_images(1, 224, seed=40 + i).to(cuda) for i in range(2)]
+    with torch.no_grad():
+        serial = [model(x).clone() for x in xs]
+    outs = [[], []]
+    errors = []
+
+    def worker(k):
+        try:
+            torch.cuda.set_device(cuda)
+            s = torch.cuda.Stream(cuda)
+            with torch.no_grad(), torch.cuda.stream(s):
+                for _ in range(5):
+                    outs[k].append(model(xs[k]))
+            s.synchronize()
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(k,)) for k in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not errors, errors
+    for k in range(2):
+        assert len(outs[k]) == 5
+        for o in outs[k]:
+            torch.testing.assert_close(o, serial[k], atol=0, rtol=0)
