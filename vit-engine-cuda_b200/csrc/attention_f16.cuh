@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <math.h>
 
 #include "common.cuh"
 
@@ -62,6 +63,107 @@ __device__ __forceinline__ void f16_drain_wait(uint64_t* bar, uint32_t parity, i
       return;
     }
   }
+}
+
+// S = Q K^T for one 128-query x 64-key tile on FP16 splits (descriptors of
+// the first 16-wide K slice; a slice further is +2 in the address field): per
+// slice the two cross products lo*hi and hi*lo first, then the first hi*hi
+// folds them in with scale-input-d (D = A*B + D*2^-11) and the rest follow.
+__device__ __forceinline__ void issue_s_f16(uint32_t d, uint64_t qh, uint64_t ql, uint64_t kh,
+                                            uint64_t kl, uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint64_t o = static_cast<uint64_t>(2 * kk);
+    umma_f16(d, ql + o, kh + o, idesc, kk ? 1u : 0u);  // lo * hi
+    umma_f16(d, qh + o, kl + o, idesc, 1u);            // hi * lo
+  }
+  umma_f16_sd11(d, qh, kh, idesc);  // hi * hi + cross * 2^-11
+#pragma unroll
+  for (int kk = 1; kk < 4; ++kk) {
+    const uint64_t o = static_cast<uint64_t>(2 * kk);
+    umma_f16(d, qh + o, kh + o, idesc, 1u);            // hi * hi
+  }
+}
+
+// O_j = P V for one tile with P's FP16 split in TMEM (hi words at p_hi, lo
+// at p_lo; two halves per 32-bit column) as the A operand, same product order.
+__device__ __forceinline__ void issue_pv_f16(uint32_t d, uint32_t p_hi, uint32_t p_lo, uint64_t vh,
+                                             uint64_t vl, uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint64_t o = static_cast<uint64_t>(2 * kk);
+    const uint32_t col = static_cast<uint32_t>(kk * 8);
+    umma_f16_tmem_a(d, p_lo + col, vh + o, idesc, kk ? 1u : 0u);  // lo * hi
+    umma_f16_tmem_a(d, p_hi + col, vl + o, idesc, 1u);            // hi * lo
+  }
+  umma_f16_tmem_a_sd11(d, p_hi, vh, idesc);  // hi * hi + cross * 2^-11
+#pragma unroll
+  for (int kk = 1; kk < 4; ++kk) {
+    const uint64_t o = static_cast<uint64_t>(2 * kk);
+    umma_f16_tmem_a(d, p_hi + kk * 8, vh + o, idesc, 1u);        // hi * hi
+  }
+}
+
+// One online-softmax step of a query row over a 64-key tile of S (s, raw
+// scores; keys from nvalid on are masked), in base 2: exp(x * scale - m) =
+// 2^(x * s_scale - m') with m' the running maximum in the same units, one FMA
+// rounding each argument. Returns the new running maximum, sets alpha (the
+// factor taking the old sums to it), updates l_run and writes P's FP16 split
+// (hi words, lo words) into ph, pl. A ragged tile of at most 16 keys (T = 197:
+// 5, T = 577: 1; uniform across the warpgroup) runs the arithmetic on 16 keys
+// only, the other 48 P entries being zero.
+__device__ __forceinline__ float softmax_tile_f16(float (&s)[64], int nvalid, float s_scale,
+                                                  float m_run, float& alpha, float& l_run,
+                                                  float (&ph)[32], float (&pl)[32]) {
+  float m_new;
+  if (nvalid <= 16) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) cmax = fmaxf(cmax, s[c]);
+    m_new = fmaxf(m_run, cmax * s_scale);
+    alpha = exp2_nonpos(m_run - m_new);
+    float psum = 0.f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      s[c] = exp2_nonpos(fmaf(s[c], s_scale, -m_new));
+      psum += s[c];
+    }
+    l_run = l_run * alpha + psum;
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      uint32_t hw = 0, lw = 0;
+      if (c < 8) h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
+      ph[c] = __uint_as_float(hw);
+      pl[c] = __uint_as_float(lw);
+    }
+  } else {
+    if (nvalid < 64) {
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
+    }
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 64; ++c) cmax = fmaxf(cmax, s[c]);
+    m_new = fmaxf(m_run, cmax * s_scale);
+    alpha = exp2_nonpos(m_run - m_new);
+    float psum = 0.f;
+#pragma unroll
+    for (int c = 0; c < 64; ++c) {
+      s[c] = exp2_nonpos(fmaf(s[c], s_scale, -m_new));
+      psum += s[c];
+    }
+    l_run = l_run * alpha + psum;
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      uint32_t hw, lw;
+      h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
+      ph[c] = __uint_as_float(hw);
+      pl[c] = __uint_as_float(lw);
+    }
+  }
+  return m_new;
 }
 
 }  // namespace

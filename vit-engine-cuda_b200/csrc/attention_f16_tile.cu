@@ -211,18 +211,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           // i.e. +2 in the descriptor's address field.
           const uint64_t kh = make_sdesc_kmajor(k_addr, 128);
           const uint64_t kl = make_sdesc_kmajor(k_addr + kPlaneKV, 128);
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint64_t o = static_cast<uint64_t>(2 * kk);
-            umma_f16(d, ql + o, kh + o, kIdescSF, kk ? 1u : 0u);  // lo * hi
-            umma_f16(d, qh + o, kl + o, kIdescSF, 1u);            // hi * lo
-          }
-          umma_f16_sd11(d, qh, kh, kIdescSF);  // hi * hi + cross * 2^-11
-#pragma unroll
-          for (int kk = 1; kk < kD / 16; ++kk) {
-            const uint64_t o = static_cast<uint64_t>(2 * kk);
-            umma_f16(d, qh + o, kh + o, kIdescSF, 1u);            // hi * hi
-          }
+          issue_s_f16(d, qh, ql, kh, kl, kIdescSF);
           umma_commit(&s_full[set]);
           return true;
         };
@@ -241,19 +230,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           const uint32_t d = p_hi + 64;
           const uint64_t vh = make_sdesc_kmajor(v_addr, 128);
           const uint64_t vl = make_sdesc_kmajor(v_addr + kPlaneKV, 128);
-#pragma unroll
-          for (int kk = 0; kk < kKV / 16; ++kk) {
-            const uint64_t o = static_cast<uint64_t>(2 * kk);
-            const uint32_t col = static_cast<uint32_t>(kk * 8);
-            umma_f16_tmem_a(d, p_lo + col, vh + o, kIdescPVF, kk ? 1u : 0u);  // lo * hi
-            umma_f16_tmem_a(d, p_hi + col, vl + o, kIdescPVF, 1u);            // hi * lo
-          }
-          umma_f16_tmem_a_sd11(d, p_hi, vh, kIdescPVF);  // hi * hi + cross * 2^-11
-#pragma unroll
-          for (int kk = 1; kk < kKV / 16; ++kk) {
-            const uint64_t o = static_cast<uint64_t>(2 * kk);
-            umma_f16_tmem_a(d, p_hi + kk * 8, vh + o, kIdescPVF, 1u);        // hi * hi
-          }
+          issue_pv_f16(d, p_hi, p_lo, vh, vl, kIdescPVF);
           umma_commit(&pv_full[set]);
           umma_commit(&kv_empty[st]);  // K_t and V_t are no longer read
           return true;
@@ -343,63 +320,11 @@ __global__ void __launch_bounds__(kThreadsF, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) s[half * 32 + c] = tt[c];
         }
-        // Online softmax in base 2: exp(x * scale - m) = 2^(x * s_scale - m'),
-        // with s_scale = scale * log2(e) (and the operand scales) and m' the
-        // running maximum in the same units; one FMA rounds each argument.
+        // P_t (and the running max / sum) from this tile's scores.
         const int nvalid = a.T - j * kKV;
-        float m_new, alpha;
-        // P's FP16 split into this set's S columns: hi words, then lo words.
+        float alpha;
         float ph[32], pl[32];
-        if (nvalid <= 16) {
-          // A ragged last tile of at most 16 keys (T = 197: 5, T = 577: 1;
-          // uniform across the warpgroup): the arithmetic covers 16 keys and
-          // the other 48 P entries are zero.
-#pragma unroll
-          for (int c = 0; c < 16; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
-          float cmax = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < 16; ++c) cmax = fmaxf(cmax, s[c]);
-          m_new = fmaxf(m_run, cmax * a.s_scale);
-          alpha = exp2_nonpos(m_run - m_new);
-          float psum = 0.f;
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            s[c] = exp2_nonpos(fmaf(s[c], a.s_scale, -m_new));
-            psum += s[c];
-          }
-          l_run = l_run * alpha + psum;
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            uint32_t hw = 0, lw = 0;
-            if (c < 8) h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
-            ph[c] = __uint_as_float(hw);
-            pl[c] = __uint_as_float(lw);
-          }
-        } else {
-          if (nvalid < kKV) {  // a ragged last tile (uniform across the warpgroup)
-#pragma unroll
-            for (int c = 0; c < kKV; ++c) s[c] = (c < nvalid) ? s[c] : -INFINITY;
-          }
-          float cmax = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < kKV; ++c) cmax = fmaxf(cmax, s[c]);
-          m_new = fmaxf(m_run, cmax * a.s_scale);
-          alpha = exp2_nonpos(m_run - m_new);
-          float psum = 0.f;
-#pragma unroll
-          for (int c = 0; c < kKV; ++c) {
-            s[c] = exp2_nonpos(fmaf(s[c], a.s_scale, -m_new));
-            psum += s[c];
-          }
-          l_run = l_run * alpha + psum;
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            uint32_t hw, lw;
-            h16_split2(s[2 * c], s[2 * c + 1], hw, lw);
-            ph[c] = __uint_as_float(hw);
-            pl[c] = __uint_as_float(lw);
-          }
-        }
+        const float m_new = softmax_tile_f16(s, nvalid, a.s_scale, m_run, alpha, l_run, ph, pl);
         __syncwarp();
         tmem_st_32x32b_x32(scol, ph);
         tmem_st_32x32b_x32(scol + 32, pl);
