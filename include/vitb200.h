@@ -105,10 +105,10 @@ int vitb200_set_gemm_variant(int variant);
  * thread-block cluster of d CTAs per tile; the other CTAs leave their fp32
  * partial tiles in their shared memory and the cluster's first CTA adds them
  * in split order over distributed shared memory (deterministic) and writes the
- * tile. With split-K off, an image's logits are bitwise identical whatever
- * batch it is in, among batches of fewer than 1024 token rows (the block GEMMs
- * then all use single-CTA tiles with the same K chunks); with it on they agree
- * to FP32 rounding. No counterpart in the reference (one CTA per 32x32 output
+ * tile. An image's logits are bitwise identical in any batch of at least 7
+ * images at 224x224 (CTA-pair tiles from 1024 token rows, no split); with
+ * split-K off also among batches of up to 5 images; otherwise they agree to
+ * FP32 rounding. No counterpart in the reference (one CTA per 32x32 output
  * tile there). Affects launches made after the call (a captured CUDA graph
  * keeps the setting it was captured with). Returns the previous setting;
  * process-wide. */

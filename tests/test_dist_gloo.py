@@ -39,7 +39,7 @@ def _worker(rank, world, port, batch, mode, queue):
             raise RuntimeError("injected failure on rank 1 before the all-gather")
         images = synthetic_images(batch, 32, seed=9)
         out = DataParallelViT(_tiny_model())(images)
-        queue.put((rank, "ok", out))
+        queue.put((rank, "ok", out.numpy()))  # pickled by value
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent, which decides
@@ -75,7 +75,7 @@ def test_gather_equals_single_process(batch):
         assert status == "ok", out
         # the CPU stand-in model's BLAS blocking depends on the slice size, so
         # compare at float64 round-off (the GPU engine is bitwise, tested on GPU)
-        torch.testing.assert_close(out, expected, atol=1e-12, rtol=1e-12)
+        torch.testing.assert_close(torch.from_numpy(out), expected, atol=1e-12, rtol=1e-12)
 
 
 def test_failed_rank_surfaces_as_error():

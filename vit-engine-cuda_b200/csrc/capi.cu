@@ -847,11 +847,12 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
   return gemm_pairs_launch(g, s);
 }
 
-// Final LayerNorm on the CLS rows only (the head reads token 0 alone), then
-// the head GEMM; up to kFusedHeadMaxBatch images one fused kernel does both
-// (CUDA-core dot products: the GEMM launch there is all latency). features /
-// logits may each be null.
-constexpr int kFusedHeadMaxBatch = 16;
+// Final LayerNorm on the CLS rows only (the head reads token 0 alone) and the
+// head: one fused kernel (CUDA-core FP32 dot products, batch invariant; at
+// batch 1 a head GEMM launch is all latency), with LayerNorm + head GEMM for
+// what it does not cover (E != 768, over 524,280 images). features / logits
+// may each be null.
+constexpr int kFusedHeadMaxBatch = 65535 * 8;
 
 int vit_head(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, const float* x,
              float* logits, float* features, int batch, cudaStream_t s) {

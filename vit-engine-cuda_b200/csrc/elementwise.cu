@@ -217,28 +217,31 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
   }
 }
 
-// Final LayerNorm of each image's CLS row fused with the classifier head, for
-// small batches (the head GEMM there is all launch latency): blockIdx.y is the
-// image; every warp loads its class's head row (the TF32 pair, hi + lo is w to
-// 2^-22) while warp 0 normalises the CLS row into shared memory with the
-// LayerNorm kernel's arithmetic (features of block 0 written out); then each
-// warp takes the FP32 dot product y . hi + y . lo plus the bias.
-constexpr int kHeadClassesPerBlock = 8;  // one per warp
+// Final LayerNorm of each image's CLS row fused with the classifier head. A
+// block serves kHeadImages images and kHeadClasses classes: every warp loads
+// its class's head row (the TF32 pair, hi + lo is w to 2^-22) into registers
+// while warp w normalises the CLS row of the block's image w into shared
+// memory with the LayerNorm kernel's arithmetic (features written out by the
+// blocks of the first class group); then each warp takes the FP32 dot products
+// y . hi + y . lo plus the bias for the block's images. Every (image, class)
+// is computed the same way whatever the batch, so the head is batch invariant.
+constexpr int kHeadImages = 8;   // one LayerNorm per warp
+constexpr int kHeadClasses = 8;  // one class per warp
 
 __global__ void __launch_bounds__(256) cls_head768_kernel(
     const float* __restrict__ x, int64_t cls_stride, const float* __restrict__ gamma,
     const float* __restrict__ beta, float eps, const float* __restrict__ w_pair,
-    const float* __restrict__ bias, int C, float* __restrict__ logits,
+    const float* __restrict__ bias, int C, int batch, float* __restrict__ logits,
     float* __restrict__ features) {
   griddep_wait();
   griddep_launch_dependents();
   constexpr int E = 768;
   constexpr int V = E / 128;
-  __shared__ __align__(16) float4 ys[E / 4];
+  __shared__ __align__(16) float4 ys[kHeadImages][E / 4];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t img = blockIdx.y;
-  const int c = blockIdx.x * kHeadClassesPerBlock + warp;
+  const int c = blockIdx.x * kHeadClasses + warp;
+  const int64_t img0 = static_cast<int64_t>(blockIdx.y) * kHeadImages;
   float4 h[V], l[V];
   if (c < C) {
     const float4* hr = reinterpret_cast<const float4*>(w_pair) + static_cast<int64_t>(c) * (E / 4);
@@ -250,8 +253,9 @@ __global__ void __launch_bounds__(256) cls_head768_kernel(
       l[i] = __ldg(lr + lane + 32 * i);
     }
   }
-  if (warp == 0) {
-    const float4* xr = reinterpret_cast<const float4*>(x + img * cls_stride);
+  const int64_t my_img = img0 + warp;
+  if (my_img < batch) {
+    const float4* xr = reinterpret_cast<const float4*>(x + my_img * cls_stride);
     float4 v[V], g[V], b[V], o[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) {
@@ -262,28 +266,34 @@ __global__ void __launch_bounds__(256) cls_head768_kernel(
     layernorm768_row(v, g, b, eps, o);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      ys[lane + 32 * i] = o[i];
+      ys[warp][lane + 32 * i] = o[i];
       if (features && blockIdx.x == 0)
-        reinterpret_cast<float4*>(features + img * E)[lane + 32 * i] = o[i];
+        reinterpret_cast<float4*>(features + my_img * E)[lane + 32 * i] = o[i];
     }
   }
   __syncthreads();
   if (c >= C) return;  // uniform across the warp
-  float acc = 0.f;
+  const float bc = __ldg(bias + c);
+#pragma unroll 1
+  for (int k = 0; k < kHeadImages; ++k) {
+    const int64_t img = img0 + k;
+    if (img >= batch) break;
+    float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const float4 y = ys[lane + 32 * i];
-    acc = fmaf(y.x, h[i].x, acc);
-    acc = fmaf(y.x, l[i].x, acc);
-    acc = fmaf(y.y, h[i].y, acc);
-    acc = fmaf(y.y, l[i].y, acc);
-    acc = fmaf(y.z, h[i].z, acc);
-    acc = fmaf(y.z, l[i].z, acc);
-    acc = fmaf(y.w, h[i].w, acc);
-    acc = fmaf(y.w, l[i].w, acc);
+    for (int i = 0; i < V; ++i) {
+      const float4 y = ys[k][lane + 32 * i];
+      acc = fmaf(y.x, h[i].x, acc);
+      acc = fmaf(y.x, l[i].x, acc);
+      acc = fmaf(y.y, h[i].y, acc);
+      acc = fmaf(y.y, l[i].y, acc);
+      acc = fmaf(y.z, h[i].z, acc);
+      acc = fmaf(y.z, l[i].z, acc);
+      acc = fmaf(y.w, h[i].w, acc);
+      acc = fmaf(y.w, l[i].w, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[img * C + c] = acc + bc;
   }
-  acc = warp_sum(acc);
-  if (lane == 0) logits[img * C + c] = acc + __ldg(bias + c);
 }
 
 int cls_head_launch(const float* x, int64_t cls_stride, const float* gamma, const float* beta,
@@ -294,9 +304,10 @@ int cls_head_launch(const float* x, int64_t cls_stride, const float* gamma, cons
       cls_stride % 4 != 0 || !al(x) || !al(gamma) || !al(beta) || !al(w_pair) ||
       (features && !al(features)))
     return VITB200_E_INVALID_ARG;
-  const dim3 grid((C + kHeadClassesPerBlock - 1) / kHeadClassesPerBlock, batch);
+  const dim3 grid((C + kHeadClasses - 1) / kHeadClasses,
+                  (batch + kHeadImages - 1) / kHeadImages);
   if (int st = launch_kernel(cls_head768_kernel, grid, dim3(256), 0, s, 1, x, cls_stride, gamma,
-                             beta, eps, w_pair, bias, C, logits, features))
+                             beta, eps, w_pair, bias, C, batch, logits, features))
     return st;
   return cuda_status(cudaGetLastError());
 }

@@ -4,8 +4,11 @@ ViT-B/16 inference shards by image: every rank holds a full replica of the
 weights (346 MB fp32 + 692 MB of TF32 pairs), runs its contiguous slice of the
 batch through the fused forward, and one NCCL all-gather assembles the logits
 on every rank. There is no other exchange: images are independent and no
-reduction crosses ranks, so the gathered logits equal the single-GPU ones bit
-for bit (each row's arithmetic does not depend on which rank computes it).
+reduction crosses ranks. From 7 images per rank (224²) every kernel's
+per-image arithmetic is the one a single GPU uses for the whole batch (CTA-pair
+GEMM tiles, the two-tile attention, the fused head), so the gathered logits
+equal the single-GPU ones bit for bit; smaller shards take the small-batch
+kernels (split K, one query tile per CTA) and agree to FP32 rounding.
 The reference project has no multi-GPU code; this module is new.
 """
 from __future__ import annotations
