@@ -108,6 +108,21 @@ def test_bad_arguments_rejected_without_gpu(call):
     assert call() == _lib.E_INVALID_ARG
 
 
+def test_diagnostic_entries_without_gpu():
+    v, d = ctypes.c_int(-1), ctypes.c_int(-1)
+    for shape in ((0, 768, 768), (197, -1, 768), (197, 768, 0)):
+        assert lib.vitb200_gemm_plan(*shape, 1, ctypes.byref(v), ctypes.byref(d)) == \
+            _lib.E_INVALID_ARG
+    assert (v.value, d.value) == (-1, -1)
+    assert lib.vitb200_check_wait_timeout(2, None) == _lib.E_INVALID_ARG
+    old = lib.vitb200_set_split_k(0)
+    try:
+        assert lib.vitb200_set_split_k(1) == 0
+        assert lib.vitb200_set_split_k(1) == 1
+    finally:
+        lib.vitb200_set_split_k(old)
+
+
 def test_workspace_too_small_rejected_without_gpu():
     assert lib.vitb200_gemm(1, 1, None, None, 1, 4, 8, 4, _lib.EPI_NONE, 1, 16,
                             None) == _lib.E_WORKSPACE

@@ -177,6 +177,7 @@ int vitb200_set_split_k(int enable) { return gemm_set_split_k(enable); }
 
 int vitb200_check_wait_timeout(int kind, void* stream) {
   VITB200_GUARD_BEGIN
+  if (kind != 0 && kind != 1) return VITB200_E_INVALID_ARG;
   if (int st = check_ready()) return st;
   return wait_timeout_launch(kind, as_stream(stream));
   VITB200_GUARD_END
