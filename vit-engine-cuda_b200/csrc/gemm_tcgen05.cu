@@ -1,5 +1,10 @@
-// TF32x3 GEMM on sm_100a tensor cores: Y = epilogue(A * B^T) with A = X[M][K],
-// B = W[N][K] (PyTorch Linear layout), both given as TF32 hi/lo pairs.
+// Split-operand GEMM on sm_100a tensor cores: Y = epilogue(A * B^T) with
+// A = X[M][K], B = W[N][K] (PyTorch Linear layout), given either as TF32 hi/lo
+// pairs (kind::tf32, three TF32 products per multiply) or as FP16 splits
+// (kind::f16: A as hi, lo*2^11; W as hi, lo*2^11, hi*2^11 of W*s; three FP16
+// products, all at the 2^11 scale, undone with an exact power of two in the
+// epilogue). The TF32 description below holds for both kinds, with K slices of
+// 16 and chunks of up to 256 for FP16.
 //
 // Reference math: the opt-in CuTe kernel csrc/kernels/gemm_cute_tf32.cu:104-125
 // computes hi*hi + hi*lo + lo*hi per 32-wide K tile with mma.sync m16n8k8 and
@@ -25,6 +30,13 @@
 //    last chunk they apply bias / GELU / residual / positional add and store
 //    fp32 and/or the TF32 pair the next GEMM consumes, while the MMA issuer
 //    already fills the free chunk buffers with the next tile.
+//
+// Large problems run 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2: the
+// leader issues the MMAs, each CTA loads its own 128 rows of A and half of B).
+// Small ones (fewer tiles than half the SMs) may split K over a thread-block
+// cluster of d CTAs per tile: the others leave their partial tiles in their
+// shared memory and the first adds them in split order over distributed
+// shared memory. plan_gemm picks the tile configuration and the split.
 //
 // Every CTA loads its own tiles with plain per-CTA copies (no broadcast loads).
 #include <cuda.h>
