@@ -284,3 +284,26 @@ def test_concurrent_host_threads_match_serial(case224, cuda):
         assert len(outs[k]) == 5
         for o in outs[k]:
             torch.testing.assert_close(o, serial[k], atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("num_classes,batch", [(10, 3), (7, 9), (1, 1)])
+def test_odd_class_counts(cuda, num_classes, batch):
+    """The fused final LayerNorm + head with class counts that leave a block's
+    warps idle (8 classes and 8 images per block) and batches past one block of
+    images; logits and features against the oracle."""
+    state = synthetic_state_dict(seed=12, img_size=224, depth=1, num_classes=num_classes)
+    img = synthetic_images(batch, 224, seed=12)
+    ref, inter = orc.vit_forward(img, state, return_intermediates=True)
+    model = ViTCUDA(num_classes=num_classes,
+                    state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+        feats = model.forward_features(img.to(cuda)).double().cpu()
+        x = model.block(0, model.embed(img.to(cuda)))
+        logits, hfeats = model.head(x)
+    assert out.shape == (batch, num_classes)
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL
+    assert (feats - inter["features"]).abs().max().item() <= LOGITS_ATOL
+    torch.testing.assert_close(logits.double().cpu(), out, atol=0, rtol=0)
+    # forward_features runs the LayerNorm kernel, head() the fused one (same row routine)
+    torch.testing.assert_close(hfeats.double().cpu(), feats, atol=1e-6, rtol=0)
