@@ -703,7 +703,8 @@ size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve
 int vit_embed(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b,
               const float* img, float* x, int batch, cudaStream_t s) {
   const int D = p->embed_dim;
-  if (int st = im2col_pair_launch(img, batch, p->in_chans, p->img_h, p->img_w, b.pair_a, s))
+  if (int st = im2col_pair_launch(img, batch, p->in_chans, p->img_h, p->img_w, b.pair_a, s,
+                                  p->cls_token, p->pos_embed, x, D))
     return st;
   GemmProblem g;
   g.a_pair = b.pair_a;
@@ -718,8 +719,7 @@ int vit_embed(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
   g.epi.P = d.P;
   g.epi.T = d.T;
   g.epi.pos = p->pos_embed;
-  if (int st = gemm_pairs_launch(g, s)) return st;
-  return cls_pos_launch(p->cls_token, 0, p->pos_embed, nullptr, x, batch, d.P, D, s);
+  return gemm_pairs_launch(g, s);  // rows 1..P; im2col wrote the CLS rows
 }
 
 // One pre-LN encoder block in place on x (vit_cuda/model.py:39-60 order):

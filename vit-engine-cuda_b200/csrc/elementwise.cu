@@ -388,8 +388,11 @@ int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const floa
 // img[B][C][H][W] -> pair[2][B*P][C*256], patch vector order (c, py, px) and
 // patches row-major over the (H/16) x (W/16) grid, as the reference kernel
 // csrc/kernels/patch_embed.cu:29-44 and torch's Conv2d weight layout agree.
+// With x != null it also writes each image's CLS row of the token matrix,
+// x[b][0] = cls + pos[0] (the patch GEMM's epilogue writes rows 1..P).
 __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, int H, int W,
-                                   float* __restrict__ pair) {
+                                   float* __restrict__ pair, const float* __restrict__ cls,
+                                   const float* __restrict__ pos, float* __restrict__ x, int E) {
   griddep_wait();
   griddep_launch_dependents();
   const int gw = W / 16, gh = H / 16;
@@ -420,18 +423,28 @@ __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, 
     *reinterpret_cast<float4*>(dst + plane) = l;
     (void)gh;
   }
+  if (x != nullptr) {
+    const int64_t T = P + 1;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+         i < static_cast<int64_t>(B) * E; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t b = i / E;
+      const int n = static_cast<int>(i - b * E);
+      x[b * T * E + n] = cls[n] + pos[n];
+    }
+  }
 }
 
 int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair,
-                       cudaStream_t s) {
-  if (B < 0 || C <= 0 || H <= 0 || W <= 0 || H % 16 || W % 16 || !img || !pair)
+                       cudaStream_t s, const float* cls, const float* pos, float* x, int E) {
+  if (B < 0 || C <= 0 || H <= 0 || W <= 0 || H % 16 || W % 16 || !img || !pair ||
+      (x && (!cls || !pos || E <= 0)))
     return VITB200_E_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(img) % 16 || reinterpret_cast<uintptr_t>(pair) % 16)
     return VITB200_E_ALIGNMENT;
   if (B == 0) return 0;
   const int64_t work = static_cast<int64_t>(B) * (H / 16) * (W / 16) * C * 64;
   if (int st_ = launch_kernel(im2col_pair_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, 1,
-      img, B, C, H, W, pair))
+      img, B, C, H, W, pair, cls, pos, x, E))
     return st_;
   return cuda_status(cudaGetLastError());
 }
