@@ -78,6 +78,8 @@ def parse_args():
     ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-p50", action="store_true")
+    ap.add_argument("--cpu-p50-runs", type=int, default=20,
+                    help="single-image CPU oracle forwards behind the CPU p50 latency")
     ap.add_argument("--mode", choices=["full", "roofline", "peaks"], default="full",
                     help="roofline: time only the dominant GEMM launch (for ncu captures); "
                          "peaks: measure cuBLAS TF32 / bf16 / fp16 GEMM throughput")
@@ -312,6 +314,31 @@ def cpu_oracle_p50_bs1(img_size: int, runs: int = 20) -> float:
     return statistics.median(times)
 
 
+def input_bytes(batch: int, img: int) -> int:
+    """Bytes of one step's images on one GPU ([batch, 3, img, img] fp32)."""
+    return batch * 3 * img * img * 4
+
+
+def flush_bytes(batch: int, img: int) -> int:
+    """L2 flush buffer of a step whose input fits in L2 (twice L2), else 0."""
+    return 2 * L2_BYTES if input_bytes(batch, img) < L2_BYTES else 0
+
+
+def workload_config(name: str, world: int) -> dict:
+    """The `config` both arms report for workload `name` on `world` GPUs."""
+    batch, img = CONFIGS[name]
+    h2d = input_bytes(batch, img)
+    fb = flush_bytes(batch, img)
+    return {"workload": name, "model": "ViT-B/16 (random init, seed 0)",
+            "global_batch": batch * world, "img_size": img, "seq_len": (img // 16) ** 2 + 1,
+            "parallelism": f"dp{world}" if world > 1 else "single GPU",
+            "l2": ("inputs larger than L2 (%.0f MB per GPU per step)" % (h2d / 1e6) if fb == 0
+                   else "L2 flushed before every timed step (%.0f MB written, outside the "
+                        "per-step CUDA events); input %.1f MB per GPU per step"
+                        % (fb / 1e6, h2d / 1e6)),
+            "gflop_per_image": GFLOP_PER_IMG.get(img)}
+
+
 # ----------------------------------------------------------------- arms
 def run_reference(args):
     rank, _, world = dist_env()
@@ -333,17 +360,20 @@ def run_reference(args):
     rate = args.cpu_sample * args.steps / dt
     sample = (f"{args.cpu_sample} images per step of the {args.config} workload "
               f"({img}x{img}, fp32), CPU oracle port of the reference path")
+    config = workload_config(args.config, world)
+    config["cpu_sample"] = (f"each step times {args.cpu_sample} of the {batch * world} images "
+                            f"on the host cores ({torch.get_num_threads()} threads)")
     emit({
         "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, "global_batch": batch * world, "img_size": img,
-                   "seq_len": (img // 16) ** 2 + 1, "parallelism": "host cores"},
+        "config": config,
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "p50_bs1_ms": {"cpu_ms": cpu_oracle_p50_bs1(img), "runs": 20},
+        "p50_bs1_ms": {"cpu_ms": cpu_oracle_p50_bs1(img, args.cpu_p50_runs),
+                       "runs": args.cpu_p50_runs},
     })
 
 
@@ -373,8 +403,8 @@ def run_ours(args):
     x_host = synthetic_images(batch, img, seed=1000 + rank)
     x_dev = x_host.to(dev)
     # A step whose input fits in L2 gets L2 flushed before it (outside the timing).
-    flush_buf = (torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
-                 if x_host.numel() * 4 < L2_BYTES else None)
+    fb = flush_bytes(batch, img)
+    flush_buf = torch.empty(fb // 4, dtype=torch.float32, device=dev) if fb else None
 
     def step_device():
         logits = model._forward_impl(x_dev)
@@ -448,16 +478,8 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, "model": "ViT-B/16 (random init, seed 0)",
-                   "global_batch": total, "img_size": img, "seq_len": T,
-                   "parallelism": f"dp{world}" if world > 1 else "single GPU",
-                   "block_gemm_operands": "+".join(operands),
-                   "l2": ("inputs larger than L2 (%.0f MB per GPU per step)" % (h2d / 1e6)
-                          if flush_buf is None else
-                          "L2 flushed before every timed step (%.0f MB written, outside the "
-                          "per-step CUDA events); input %.1f MB per GPU per step"
-                          % (flush_buf.numel() * 4 / 1e6, h2d / 1e6)),
-                   "gflop_per_image": GFLOP_PER_IMG.get(img)},
+        "config": workload_config(args.config, world),
+        "block_gemm_operands": "+".join(operands),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
         "gpu_launches": int(launches),
@@ -477,7 +499,7 @@ def run_ours(args):
             "value": rate, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{args.cpu_sample} images x {reps} reps of the {args.config} workload "
                       "(CPU oracle port of the reference path, fp32)",
-            "p50_bs1_ms": cpu_oracle_p50_bs1(img)}
+            "p50_bs1_ms": cpu_oracle_p50_bs1(img, args.cpu_p50_runs)}
     if rank == 0:
         emit(result)
     if world > 1:

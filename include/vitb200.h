@@ -177,8 +177,9 @@ int vitb200_gemm(const float* X, const float* W, const float* bias,
  * without launching. Calls share that array: calls whose GPU work can overlap
  * (unordered streams, concurrent host threads) race; calls on one stream are
  * safe. The first call on a device looks up the array's device address; make
- * it before any stream capture. Allocates nothing. It has no counterpart in
- * the reference. */
+ * it before any stream capture. That address is kept for the life of the
+ * process, so do not call this again on a device after cudaDeviceReset.
+ * Allocates nothing. It has no counterpart in the reference. */
 int vitb200_gemm_noalloc(const float* X, const float* W, const float* bias,
                          const float* residual, float* Y, int64_t M, int K, int N,
                          int epilogue, void* stream);

@@ -84,6 +84,22 @@ def test_blocks_teacher_forced(case224, cuda):
         assert orc.rel_l2(y.cpu(), xout) <= BLOCK_REL_L2, i
 
 
+def test_op_by_op_block_matches_oracle(case224, cuda):
+    """The reference's own block surface, ViTBlockCUDA.forward (reference
+    vit_cuda/model.py:39-60: the eight registered ops one by one, residual adds
+    in PyTorch), against the oracle's block on the same tokens (B=2, T=197):
+    every block fed the oracle's input, relative L2 within the per-block bar."""
+    _, _, _, inter, model = case224
+    inputs = [inter["embed"]] + inter["blocks"][:-1]
+    worst = 0.0
+    with torch.no_grad():
+        for i, (xin, xout) in enumerate(zip(inputs, inter["blocks"])):
+            y = model.blocks[i](xin.float().to(cuda), model.scale, model.eps)
+            assert y.shape == xin.shape
+            worst = max(worst, orc.rel_l2(y.cpu(), xout))
+    assert worst <= BLOCK_REL_L2, worst
+
+
 def test_forward_features(case224, cuda):
     _, img, _, inter, model = case224
     with torch.no_grad():
@@ -167,16 +183,63 @@ def test_graph_matches_eager(cuda):
     torch.testing.assert_close(g2, e2, atol=0, rtol=0)
 
 
-def test_384_tokens577(cuda):
+def test_384_tokens577(case384, cuda):
     """384x384 input, T = 577 (the reference's kernels hardcode 224/197)."""
-    state = synthetic_state_dict(seed=1, img_size=384)
-    img = synthetic_images(1, 384, seed=1)
-    ref = orc.vit_forward(img, state)
-    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    _, img, ref, _, model = case384
     with torch.no_grad():
         out = model(img.to(cuda)).double().cpu()
     assert (out - ref).abs().max().item() <= LOGITS_ATOL
     assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
+@pytest.fixture(scope="module")
+def case384(cuda):
+    state = synthetic_state_dict(seed=1, img_size=384)
+    img = synthetic_images(1, 384, seed=1)
+    logits, inter = orc.vit_forward(img, state, return_intermediates=True)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    return state, img, logits, inter, model
+
+
+def test_384_blocks_chained_and_teacher_forced(case384, cuda):
+    """384x384, T = 577 (five query tiles, ten key tiles): per-block relative
+    L2 of the fused path, run block by block from its own embedding (chained)
+    and with each block fed the oracle's input (teacher-forced)."""
+    _, img, ref_logits, inter, model = case384
+    x = model.embed(img.to(cuda))
+    assert orc.rel_l2(x.cpu(), inter["embed"]) <= BLOCK_REL_L2
+    chained = 0.0
+    for i, ref_block in enumerate(inter["blocks"]):
+        x = model.block(i, x)
+        chained = max(chained, orc.rel_l2(x.cpu(), ref_block))
+    assert chained <= BLOCK_REL_L2, chained
+    logits, _ = model.head(x)
+    assert (logits.double().cpu() - ref_logits).abs().max().item() <= LOGITS_ATOL
+    inputs = [inter["embed"]] + inter["blocks"][:-1]
+    forced = 0.0
+    for i, (xin, xout) in enumerate(zip(inputs, inter["blocks"])):
+        forced = max(forced, orc.rel_l2(model.block(i, xin.float().to(cuda)).cpu(), xout))
+    assert forced <= BLOCK_REL_L2, forced
+
+
+def test_cfg5_shard_batch512_384(case384, cuda):
+    """BASELINE configs[4]'s per-GPU shard: 512 images at 384x384 (T = 577,
+    295,424 token rows) in one forward. Three images of the batch (first,
+    middle, last) against the oracle; the same images alone in a batch of 7
+    give bitwise the same logits (the per-image arithmetic does not depend on
+    the batch from 7 images up), so every shard of the 4096-image batch
+    computes what one GPU would."""
+    state, _, _, _, model = case384
+    x = synthetic_images(512, 384, seed=4096)
+    rows = [0, 255, 511]
+    with torch.no_grad():
+        out = model(x.to(cuda)).double().cpu()
+        small = model(x[rows + [1, 2, 3, 4]].to(cuda)).double().cpu()
+    assert out.shape == (512, 1000) and torch.isfinite(out).all()
+    torch.testing.assert_close(out[rows], small[:3], atol=0, rtol=0)
+    ref = orc.vit_forward(x[rows], state)
+    assert (out[rows] - ref).abs().max().item() <= LOGITS_ATOL
+    assert torch.equal(out[rows].argmax(-1), ref.argmax(-1))
 
 
 def test_operand_choice(case224, cuda):
@@ -233,6 +296,28 @@ def test_streamed_inference_matches_eager(cuda):
     with torch.no_grad():
         for x, o in zip(batches, outs):
             torch.testing.assert_close(o, model(x.to(cuda)).cpu(), atol=0, rtol=0)
+
+
+def test_streamed_inference_host_buffer_reuse(cuda):
+    """One pinned host buffer refilled between calls: after waiting on
+    input_copied() the buffer may be overwritten, and each call's logits are
+    those of the images it held when it was called."""
+    import vit_cuda
+    state = synthetic_state_dict(seed=3, img_size=224)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    batches = [synthetic_images(2, 224, seed=60 + i) for i in range(4)]
+    host = torch.empty(2, 3, 224, 224).pin_memory()
+    run = vit_cuda.StreamedInference(model, (2, 3, 224, 224))
+    assert run.input_copied() is None
+    outs = []
+    for b in batches:
+        host.copy_(b)
+        outs.append(run(host, torch.empty(2, 1000).pin_memory()))
+        run.input_copied().synchronize()
+    torch.cuda.current_stream().synchronize()
+    with torch.no_grad():
+        for b, o in zip(batches, outs):
+            torch.testing.assert_close(o, model(b.to(cuda)).cpu(), atol=0, rtol=0)
 
 
 def test_batch_invariance_from_seven_images(case224, cuda):

@@ -61,3 +61,13 @@ def test_noalloc_rejects_oversize(vlib, cuda):
                                        4096, 1024, 1024, vlib.EPI_NONE,
                                        torch.cuda.current_stream().cuda_stream)
     assert st == vlib.E_WORKSPACE
+
+
+def test_noalloc_rejects_sizes_that_would_wrap(vlib, cuda):
+    # M * Kp overflows 64 bits: rejected by the size check, nothing launched.
+    x = torch.empty(1, 4, device=cuda)
+    for m, k, n in (((1 << 62), 1024, 16), (16, 1024, (1 << 31) - 1)):
+        st = vlib.lib.vitb200_gemm_noalloc(x.data_ptr(), x.data_ptr(), None, None, x.data_ptr(),
+                                           m, k, n, vlib.EPI_NONE,
+                                           torch.cuda.current_stream().cuda_stream)
+        assert st == vlib.E_WORKSPACE

@@ -24,7 +24,9 @@
 //    GEMM reads, including the zero padding of K up to Kp.
 //  * the first call on a device resolves the array's device address (set-up,
 //    see scratch_on_current_device); make that first call before any stream
-//    capture begins.
+//    capture begins. The address is cached per device ordinal for the life of
+//    the process: after a cudaDeviceReset the cached address is stale, so a
+//    process that resets a device must not call this entry point on it again.
 #include <mutex>
 
 #include "engine.h"
@@ -80,7 +82,12 @@ extern "C" int vitb200_gemm_noalloc(const float* X, const float* W, const float*
         (epilogue == VITB200_EPI_BIAS_RESID && !residual))
       return VITB200_E_INVALID_ARG;
     if (!Y || (K > 0 && (!X || !W))) return VITB200_E_INVALID_ARG;
+    // Size check before any multiplication that could wrap: each of X's and
+    // W's pairs must fit in the array on its own before the sum is formed.
     const size_t Kp = (static_cast<size_t>(K) + 3) / 4 * 4;
+    const size_t half = kScratchFloats / 2;
+    if (Kp > 0 && (static_cast<size_t>(M) > half / Kp || static_cast<size_t>(N) > half / Kp))
+      return VITB200_E_WORKSPACE;
     const size_t a_floats = round_up(2 * static_cast<size_t>(M) * Kp, 64);
     const size_t need = a_floats + 2 * static_cast<size_t>(N) * Kp;
     if (need > kScratchFloats) return VITB200_E_WORKSPACE;

@@ -3,11 +3,15 @@
 The library is the product path: there is no fallback. Importing this module
 raises ImportError when the library has not been built (run
 ``python vit-engine-cuda_b200/build.py`` or ``__graft_entry__.build()``).
+The shared object itself is opened on the first call into it, so a process
+that imports the package only for its host-side helpers (the seeded
+synthetic weights of ``vit_cuda.weights``, say) never maps it.
 """
 from __future__ import annotations
 
 import ctypes
 import os
+import threading
 from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libvitb200.so")
@@ -111,20 +115,53 @@ _SIGNATURES = {
 }
 
 
+def _missing() -> ImportError:
+    return ImportError(
+        f"vit_cuda: {LIB_PATH} is missing; build it with "
+        "`python vit-engine-cuda_b200/build.py` (there is no CPU fallback)")
+
+
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
-        raise ImportError(
-            f"vit_cuda: {LIB_PATH} is missing; build it with "
-            "`python vit-engine-cuda_b200/build.py` (there is no CPU fallback)")
-    lib = ctypes.CDLL(LIB_PATH)
+        raise _missing()
+    cdll = ctypes.CDLL(LIB_PATH)
     for name, (restype, argtypes) in _SIGNATURES.items():
-        fn = getattr(lib, name)
+        fn = getattr(cdll, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    return lib
+    return cdll
 
 
-lib = _load()
+class _Library:
+    """libvitb200.so, opened (and its signatures declared) on the first
+    attribute access; each entry point is then cached on this object, so later
+    calls cost a plain attribute lookup."""
+
+    def __init__(self):
+        self._cdll = None
+        self._lock = threading.Lock()
+
+    def _open(self) -> ctypes.CDLL:
+        with self._lock:
+            if self._cdll is None:
+                self._cdll = _load()
+            return self._cdll
+
+    @property
+    def loaded(self) -> bool:
+        return self._cdll is not None
+
+    def __getattr__(self, name: str):
+        if name.startswith("__"):
+            raise AttributeError(name)
+        fn = getattr(self._open(), name)
+        self.__dict__[name] = fn
+        return fn
+
+
+if not os.path.exists(LIB_PATH):
+    raise _missing()
+lib = _Library()
 
 
 def status_string(status: int) -> str:

@@ -20,7 +20,12 @@ class StreamedInference:
     """``run = StreamedInference(model, (B, 3, H, W)); out = run(x_pinned)``
     enqueues one batch and returns the pinned host tensor its logits will land
     in (valid once the current stream is synchronised). ``fn`` replaces the
-    forward (default ``model``), e.g. to all-gather logits across ranks."""
+    forward (default ``model``), e.g. to all-gather logits across ranks.
+
+    The call returns before the batch has left host memory: the copy from
+    ``x_host`` runs asynchronously on the copy stream. ``x_host`` must not be
+    modified until that copy is done — wait on ``input_copied()`` (or for the
+    logits, which come later) before refilling the same host buffer."""
 
     def __init__(self, model, batch_shape, fn: Optional[Callable] = None):
         self.model = model
@@ -32,6 +37,13 @@ class StreamedInference:
         self.copied = [torch.cuda.Event() for _ in range(2)]
         self.consumed = [torch.cuda.Event() for _ in range(2)]
         self.i = 0
+        self.last = None
+
+    def input_copied(self) -> Optional[torch.cuda.Event]:
+        """The event recorded after the latest call's host-to-device copy: once
+        it has completed (``.synchronize()`` / ``.query()``), that call's host
+        input may be overwritten. None before the first call."""
+        return None if self.last is None else self.copied[self.last]
 
     def __call__(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None):
         if x_host.device.type != "cpu":
@@ -50,6 +62,7 @@ class StreamedInference:
         with torch.no_grad():
             logits = self.fn(buf)
         self.consumed[k].record(compute)
+        self.last = k
         if out_host is None:
             out_host = torch.empty(tuple(logits.shape), dtype=logits.dtype, pin_memory=True)
         out_host.copy_(logits, non_blocking=True)
