@@ -80,10 +80,14 @@ def parse_args():
     ap.add_argument("--no-p50", action="store_true")
     ap.add_argument("--cpu-p50-runs", type=int, default=20,
                     help="single-image CPU oracle forwards behind the CPU p50 latency")
-    ap.add_argument("--mode", choices=["full", "roofline", "peaks"], default="full",
+    ap.add_argument("--mode", choices=["full", "roofline", "peaks", "forward"], default="full",
                     help="roofline: time only the dominant GEMM launch (for ncu captures); "
-                         "peaks: measure cuBLAS TF32 / bf16 / fp16 GEMM throughput")
+                         "peaks: measure cuBLAS TF32 / bf16 / fp16 GEMM throughput; "
+                         "forward: only model forwards of --batch images (for profilers)")
     ap.add_argument("--batch", type=int, default=None, help="override images per GPU")
+    ap.add_argument("--weights", choices=["init", "trained"], default="init",
+                    help="synthetic weight statistics: timm's initialisation (default) or "
+                         "trained-like (wider LayerNorm gains, heavier weight rows)")
     ap.add_argument("--kernel", choices=sorted(ROOFLINE_GEMMS) + ["attention", "attention_tf32",
                                                                  "patch"], default="fc1",
                     help="roofline mode: which block GEMM (FP16 splits), the FP16-split "
@@ -324,12 +328,14 @@ def flush_bytes(batch: int, img: int) -> int:
     return 2 * L2_BYTES if input_bytes(batch, img) < L2_BYTES else 0
 
 
-def workload_config(name: str, world: int) -> dict:
+def workload_config(name: str, world: int, weights: str = "init") -> dict:
     """The `config` both arms report for workload `name` on `world` GPUs."""
     batch, img = CONFIGS[name]
     h2d = input_bytes(batch, img)
     fb = flush_bytes(batch, img)
-    return {"workload": name, "model": "ViT-B/16 (random init, seed 0)",
+    model = ("ViT-B/16 (random init, seed 0)" if weights == "init" else
+             "ViT-B/16 (random init reshaped to trained-like statistics, seed 0)")
+    return {"workload": name, "model": model,
             "global_batch": batch * world, "img_size": img, "seq_len": (img // 16) ** 2 + 1,
             "parallelism": f"dp{world}" if world > 1 else "single GPU",
             "l2": ("inputs larger than L2 (%.0f MB per GPU per step)" % (h2d / 1e6) if fb == 0
@@ -348,7 +354,7 @@ def run_reference(args):
     from oracle import vit_oracle
     from vit_cuda.weights import synthetic_images, synthetic_state_dict
     torch.set_num_threads(os.cpu_count() or 1)
-    state = synthetic_state_dict(seed=0, img_size=img)
+    state = synthetic_state_dict(seed=0, img_size=img, stats=args.weights)
     x = synthetic_images(args.cpu_sample, img, seed=0)
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -360,7 +366,7 @@ def run_reference(args):
     rate = args.cpu_sample * args.steps / dt
     sample = (f"{args.cpu_sample} images per step of the {args.config} workload "
               f"({img}x{img}, fp32), CPU oracle port of the reference path")
-    config = workload_config(args.config, world)
+    config = workload_config(args.config, world, args.weights)
     config["cpu_sample"] = (f"each step times {args.cpu_sample} of the {batch * world} images "
                             f"on the host cores ({torch.get_num_threads()} threads)")
     emit({
@@ -396,7 +402,7 @@ def run_ours(args):
     batch, img = CONFIGS[args.config]
     T = (img // 16) ** 2 + 1
     total = batch * world
-    state = synthetic_state_dict(seed=0, img_size=img)
+    state = synthetic_state_dict(seed=0, img_size=img, stats=args.weights)
     model = vit_cuda.ViTCUDA(state_dict={k: v.to(dev) for k, v in state.items()}).to(dev).eval()
     model.prepare()
     operands = sorted({k for blk in model.gemm_operands for k in blk.values()})
@@ -478,7 +484,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args.config, world),
+        "config": workload_config(args.config, world, args.weights),
         "block_gemm_operands": "+".join(operands),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
@@ -625,6 +631,37 @@ def run_roofline_only(args):
           "kernel_ms": ms, "f16_pipe_tflops": 3 * 2.0 * M * N * K / (ms * 1e-3) / 1e12})
 
 
+def run_forward_only(args):
+    """`warmup` + `steps` forwards of the model on `batch` images of the
+    config's size, nothing else (a small case for profilers); prints one JSON
+    line with the median CUDA-event time per forward."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    import vit_cuda
+    from vit_cuda.weights import synthetic_images, synthetic_state_dict
+    batch, img = CONFIGS[args.config]
+    if args.batch:
+        batch = args.batch
+    state = synthetic_state_dict(seed=0, img_size=img, stats=args.weights)
+    model = vit_cuda.ViTCUDA(state_dict={k: v.to(dev) for k, v in state.items()}).to(dev).eval()
+    x = synthetic_images(batch, img, seed=1).to(dev)
+    times = []
+    with torch.no_grad():
+        for i in range(args.warmup + args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            model(x)
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                times.append(e0.elapsed_time(e1))
+    from vit_cuda import _lib
+    assert _lib.device_error() == 0, "a kernel reported a device error"
+    emit({"mode": "forward", "workload": args.config, "batch": batch,
+          "ms_per_forward": statistics.median(times) if times else None})
+
+
 def run_peaks():
     """Dense tensor throughput of cuBLAS (torch.matmul) at 8192^3 on this GPU:
     TF32 (fp32 inputs with TF32 allowed), bf16 and fp16; burst = best of 10
@@ -682,6 +719,9 @@ def main():
         return
     if args.mode == "roofline":
         run_roofline_only(args)
+        return
+    if args.mode == "forward":
+        run_forward_only(args)
         return
     if args.batch:
         CONFIGS[args.config] = (args.batch, CONFIGS[args.config][1])

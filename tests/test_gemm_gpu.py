@@ -180,3 +180,32 @@ def test_bad_arguments(vlib, cuda):
     # misaligned pair pointer
     assert lib.vitb200_gemm_pairs(x.data_ptr() + 4, x.data_ptr(), None, None, y.data_ptr(), 4,
                                   None, 1, 4, 4, vlib.EPI_NONE, s) == vlib.E_ALIGNMENT
+
+
+def test_gelu_epilogue_accuracy(vlib, cuda):
+    """The GEMM epilogue's GELU (a fitted polynomial for the normal tail and one
+    ex2; no erff) against float64 GELU and against torch's fp32 GELU on the
+    GPU: X holds 16,384 values over [-12, 12] plus tiny ones, W = I, so
+    Y = GELU(X) up to the TF32x3 identity product (2^-22 relative)."""
+    torch.manual_seed(7)
+    k = 256
+    vals = torch.cat([torch.linspace(-12, 12, 64 * k - 2 * k),
+                      torch.logspace(-30, 0, k) * torch.sign(torch.randn(k)),
+                      torch.randn(k) * 3])
+    x = vals.view(64, k).to(cuda)
+    w = torch.eye(k, device=cuda)
+    b = torch.zeros(k, device=cuda)
+    y = run_gemm(vlib, x, w, b, None, "gelu").double()
+    x64 = x.double()
+    g64 = F.gelu(x64, approximate="none")
+    err = (y - g64).abs()
+    assert (err <= 2.5e-6 * x64.abs() + 1e-37).all(), err.max().item()
+    g32 = F.gelu(x, approximate="none").double()  # CUDA's erff-based GELU in fp32
+    assert ((y - g32).abs() <= 3e-6 * x64.abs() + 1e-37).all()
+    # FP16-split path: same epilogue code, bounded inputs
+    from test_gemm_f16_gpu import run_f16
+    xs = (x[:, :] / 2).contiguous()
+    yf = run_f16(vlib, xs, w, b, None, "gelu").double()
+    gf = F.gelu(xs.double(), approximate="none")
+    # (the FP16 split itself is exact to 2^-22 relative + 2^-36 absolute)
+    assert ((yf - gf).abs() <= 2.5e-6 * xs.double().abs() + 1e-10).all()

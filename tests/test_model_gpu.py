@@ -392,3 +392,31 @@ def test_odd_class_counts(cuda, num_classes, batch):
     torch.testing.assert_close(logits.double().cpu(), out, atol=0, rtol=0)
     # forward_features runs the LayerNorm kernel, head() the fused one (same row routine)
     torch.testing.assert_close(hfeats.double().cpu(), feats, atol=1e-6, rtol=0)
+
+
+def test_trained_like_weights(cuda):
+    """Weights with trained-like statistics (LayerNorm gains spread to 5-10,
+    twice-wider weights with heavy rows, larger positional embeddings): the
+    worst-case input bounds stay inside the FP16 split's range (block 11's
+    largest, the attention's v, is ~1.4e4 against 3.3e4), so every block GEMM
+    and attention keeps the FP16 path, and the forward still meets the parity
+    bar, block by block and on the logits."""
+    from vit_cuda.split import F16_SAFE_BOUND, block_input_bounds
+    state = synthetic_state_dict(seed=0, img_size=224, stats="trained")
+    img = synthetic_images(2, 224, seed=0)
+    ref, inter = orc.vit_forward(img, state, return_intermediates=True)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    model.prepare()
+    worst = max(max(block_input_bounds(b, 768).values()) for b in model.blocks)
+    assert worst < F16_SAFE_BOUND
+    assert all(k == "f16" for blk in model.gemm_operands for k in blk.values())
+    x = model.embed(img.to(cuda))
+    chained = 0.0
+    for i, ref_block in enumerate(inter["blocks"]):
+        x = model.block(i, x)
+        chained = max(chained, orc.rel_l2(x.cpu(), ref_block))
+    assert chained <= BLOCK_REL_L2, chained
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))

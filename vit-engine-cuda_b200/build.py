@@ -70,7 +70,7 @@ def compile_one(src: str) -> tuple[str, str]:
 # per-thread register count their split assumes. csrc/attention_f16.cu and
 # csrc/attention_f16_tile.cu: 384 threads launched at 168. csrc/gemm_tcgen05.cu: the last template argument
 # (EPI, the number of epilogue warpgroups) sets it: 2 -> 384 threads at 168,
-# 4 -> 640 threads at 96 (EpiCfg there). A kernel compiled to any other count
+# 3 -> 512 threads at 128, 4 -> 640 threads at 96 (EpiCfg there). A kernel compiled to any other count
 # could make setmaxnreg.inc wait forever.
 def expected_registers(mangled: str) -> int | None:
     if "attention_f16_kernel" in mangled or "attention_f16_tile_kernel" in mangled:
@@ -78,7 +78,7 @@ def expected_registers(mangled: str) -> int | None:
     m = re.search(r"gemm_tf32x3_kernelI(.*?)EEv", mangled)
     if m:
         epi = int(re.findall(r"Li(\d+)E", m.group(1) + "E")[-1])
-        return {2: 168, 4: 96}[epi]
+        return {2: 168, 3: 128, 4: 96}[epi]
     return None
 
 

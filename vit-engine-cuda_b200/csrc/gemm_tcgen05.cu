@@ -79,21 +79,25 @@ constexpr int kBM = 128;
 constexpr int kStgWords = 32 * 32;
 __device__ __forceinline__ int stg_at(int r, int q) { return r * 32 + 4 * (q ^ (r & 7)); }
 // Warpgroup 0 = TMA producer, MMA issuer, two idle warps; warpgroups 1..EPI =
-// epilogue (EPI = 2 or 4). Launched at kLaunchRegs registers per thread
+// epilogue (EPI = 2, 3 or 4). Launched at kLaunchRegs registers per thread
 // (65536 / threads, rounded down to 8), then warpgroup 0 gives registers up
 // (kCtrlRegs) and the epilogue warpgroups take them (kEpiRegs):
 //   EPI 2: 384 threads at 168: 128 * 56 + 256 * 224 = 64512 = 384 * 168
+//   EPI 3: 512 threads at 128: 128 * 32 + 384 * 160 = 65536 = 512 * 128
 //   EPI 4: 640 threads at  96: 128 * 56 + 512 * 104 = 60416 <= 640 * 96
 // build.py checks that ptxas allocated exactly kLaunchRegs to each instance.
-// Every compiled configuration uses EPI = 2: four epilogue warpgroups halve
-// each thread's columns but, at 104 registers, spill and ran 12-20 % slower.
+// The epilogue warpgroups take the tile's 32-column slabs round robin (slab s
+// to warpgroup s % EPI). Every compiled configuration uses EPI = 2: four
+// epilogue warpgroups, at 104 registers, spilled and ran 12-20 % slower, and
+// three (CTA-pair tiles, 96 columns per thread at 160 registers) spilled too
+// and ran 5-8 % slower on all four block GEMMs.
 template <int EPI>
 struct EpiCfg {
   static constexpr int kThreads = 128 * (1 + EPI);
-  static constexpr uint32_t kLaunchRegs = EPI == 2 ? 168 : 96;
-  static constexpr uint32_t kCtrlRegs = 56;
-  static constexpr uint32_t kEpiRegs = EPI == 2 ? 224 : 104;
-  static_assert(EPI == 2 || EPI == 4, "epilogue warpgroups");
+  static constexpr uint32_t kLaunchRegs = EPI == 2 ? 168 : (EPI == 3 ? 128 : 96);
+  static constexpr uint32_t kCtrlRegs = EPI == 3 ? 32 : 56;
+  static constexpr uint32_t kEpiRegs = EPI == 2 ? 224 : (EPI == 3 ? 160 : 104);
+  static_assert(EPI >= 2 && EPI <= 4, "epilogue warpgroups");
   static_assert(128 * kCtrlRegs + 128 * EPI * kEpiRegs <= kThreads * kLaunchRegs,
                 "register split exceeds the launch allocation");
   static_assert(kThreads * kLaunchRegs <= 65536, "registers");
@@ -128,8 +132,9 @@ struct GemmCfg {
   static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + 1024;
   static constexpr int kNumBufs = kTmemAll / BN;  // chunk accumulators in TMEM
   static constexpr int kTmemCols = kTmemAll;
-  static constexpr int kHalfN = BN / EPI;         // columns per epilogue warpgroup
-  static_assert(kHalfN % 32 == 0, "epilogue columns per warpgroup");
+  static constexpr int kSlabs = BN / 32;          // 32-column slabs of a tile
+  static constexpr int kWgSlabs = (kSlabs + EPI - 1) / EPI;  // slabs per epilogue warpgroup (max)
+  static constexpr int kWgCols = 32 * kWgSlabs;   // FP32 sums per epilogue thread
   static constexpr int kTileM = PAIR ? 2 * kBM : kBM;
   static constexpr uint32_t kIdesc = F16 ? make_idesc_f16(kTileM, BN) : make_idesc_tf32(kTileM, BN);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -681,11 +686,10 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
     setmaxnreg_inc<Epi::kEpiRegs>();
     // ------------------------------------------------------------ epilogue
     // Warps 4 .. 4 + 4*EPI - 1: warp w reads TMEM lanes [32*(w%4), +32) (one
-    // output row per thread); epilogue warpgroup `wg` owns columns
-    // [wg*BN/EPI, +BN/EPI).
+    // output row per thread); epilogue warpgroup `wg` owns the tile's slabs
+    // wg, wg + EPI, wg + 2*EPI, ... (32 columns each).
     const int wg = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int col0 = wg * Cfg::kHalfN;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     float* stg = reinterpret_cast<float*>(ring + STAGES * Cfg::kStageBytes) +
                  (warp - 4) * kStgWords;
@@ -696,9 +700,9 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       const int split = w - tile * ksplit;
       const int m_blk = tile / args.num_n_tiles;
       const int n_blk = tile - m_blk * args.num_n_tiles;
-      float sum[Cfg::kHalfN];
+      float sum[Cfg::kWgCols];
 #pragma unroll
-      for (int c = 0; c < Cfg::kHalfN; ++c) sum[c] = 0.f;
+      for (int c = 0; c < Cfg::kWgCols; ++c) sum[c] = 0.f;
       for (int j = 0; j < num_chunks; ++j) {
         int buf;
         uint32_t use;
@@ -709,12 +713,19 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < Cfg::kHalfN / 16; ++q) {
-          float part[16];
-          __syncwarp();
-          tmem_ld_32x32b_x16(lane_base + static_cast<uint32_t>(buf * BN + col0 + q * 16), part);
+        for (int i = 0; i < Cfg::kWgSlabs; ++i) {
+          const int slab = wg + EPI * i;
+          if (Cfg::kSlabs % EPI == 0 || slab < Cfg::kSlabs) {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) sum[q * 16 + c] += part[c];
+            for (int h = 0; h < 2; ++h) {
+              float part[16];
+              __syncwarp();
+              tmem_ld_32x32b_x16(
+                  lane_base + static_cast<uint32_t>(buf * BN + slab * 32 + h * 16), part);
+#pragma unroll
+              for (int c = 0; c < 16; ++c) sum[i * 32 + h * 16 + c] += part[c];
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -733,14 +744,14 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
           // cluster rank). The others leave their partial sums in their own
           // stage ring, idle now that their last MMA has completed; the leader
           // (split 0) adds them in split order over distributed shared memory
-          // (deterministic) and finishes the tile. Layout [slab][c / 4][lane]
+          // (deterministic) and finishes the tile. Layout [warp][c / 4][lane]
           // of float4: each warp access is 512 contiguous bytes.
           const int slab = warp - 4;
-          float4* part = reinterpret_cast<float4*>(ring) + slab * (Cfg::kHalfN / 4) * 32 + lane;
+          float4* part = reinterpret_cast<float4*>(ring) + slab * (Cfg::kWgCols / 4) * 32 + lane;
           if (split != 0) {
             fence_proxy_async_smem();
 #pragma unroll
-            for (int c = 0; c < Cfg::kHalfN; c += 4)
+            for (int c = 0; c < Cfg::kWgCols; c += 4)
               part[(c / 4) * 32] = make_float4(sum[c], sum[c + 1], sum[c + 2], sum[c + 3]);
             mbar_arrive_cluster(mapa_shared(smem_addr(&split_bar[slab]), 0));
             continue;
@@ -754,7 +765,7 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
           for (int sp = 1; sp < ksplit; ++sp) {
             const uint32_t src = mapa_shared(part_addr, static_cast<uint32_t>(sp));
 #pragma unroll
-            for (int c = 0; c < Cfg::kHalfN; c += 4) {
+            for (int c = 0; c < Cfg::kWgCols; c += 4) {
               const float4 t = ld_shared_cluster_f4(src + static_cast<uint32_t>(c / 4) * 512u);
               sum[c] += t.x;
               sum[c + 1] += t.y;
@@ -768,17 +779,18 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       const int64_t m_base = static_cast<int64_t>(m_blk) * Cfg::kTileM +
                              static_cast<int64_t>(rank) * kBM + quarter * 32;
       if (m_base < args.M) {
-        // One copy of the slab code, not kHalfN/32: after each slab the sums
+        // One copy of the slab code, not kWgSlabs: after each slab the sums
         // move down by 32 registers, so the loop body indexes statically.
 #pragma unroll 1
-        for (int q = 0; q < Cfg::kHalfN / 32; ++q) {
-          const int n0 = n_blk * BN + col0 + q * 32;
-          if (n0 < args.N) {
+        for (int i = 0; i < Cfg::kWgSlabs; ++i) {
+          const int slab = wg + EPI * i;
+          const int n0 = n_blk * BN + slab * 32;
+          if ((Cfg::kSlabs % EPI == 0 || slab < Cfg::kSlabs) && n0 < args.N) {
             float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[0]);
             epilogue_slab<F16>(args, m_base, lane, n0, part, stg);
           }
 #pragma unroll
-          for (int c = 0; c + 32 < Cfg::kHalfN; ++c) sum[c] = sum[c + 32];
+          for (int c = 0; c + 32 < Cfg::kWgCols; ++c) sum[c] = sum[c + 32];
         }
       }
     }
@@ -1034,12 +1046,15 @@ int set_smem_attr() {
 }
 
 // A tile configuration as a type, for visitors over the variant table.
-template <int KIND_, int BN_, int BK_, int STAGES_, int CHUNK_KB_, bool PAIR_>
+template <int KIND_, int BN_, int BK_, int STAGES_, int CHUNK_KB_, bool PAIR_, int EPI_ = 2>
 struct VariantT {
   static constexpr int KIND = KIND_, BN = BN_, BK = BK_, STAGES = STAGES_, CHUNK_KB = CHUNK_KB_;
   static constexpr bool PAIR = PAIR_;
-  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, 2>;
-  static constexpr auto kernel() { return gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, 2>; }
+  static constexpr int EPI = EPI_;
+  using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
+  static constexpr auto kernel() {
+    return gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
+  }
 };
 
 // The table of tile configurations: calls f(VariantT<...>{}) for variant v
@@ -1105,7 +1120,8 @@ GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
       const int num_kb = (Kp + T::BK - 1) / T::BK;
       const int max_d = (T::PAIR || !g_split_k) ? 1 : kMaxSplit;
       for (int d = 1; d <= max_d; ++d) {
-        if (!split_fits(T::kernel(), T::Cfg::kSmemBytes, EpiCfg<2>::kThreads, tiles, num_kb, d))
+        if (!split_fits(T::kernel(), T::Cfg::kSmemBytes, EpiCfg<T::EPI>::kThreads, tiles, num_kb,
+                        d))
           continue;
         const int64_t waves = (tiles * d + sms - 1) / sms;
         const int64_t cost =
@@ -1140,7 +1156,7 @@ int gemm_prepare_device() {
   for (int v = 1; v < kNumVariants; ++v) {
     const int st = with_variant(v, [](auto t) {
       using T = decltype(t);
-      return set_smem_attr<T::KIND, T::BN, T::BK, T::STAGES, T::CHUNK_KB, T::PAIR>();
+      return set_smem_attr<T::KIND, T::BN, T::BK, T::STAGES, T::CHUNK_KB, T::PAIR, T::EPI>();
     });
     if (st) return st;
   }
@@ -1181,8 +1197,8 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
   const GemmPlan plan = plan_gemm(p.M, p.N, p.Kp, f16);
   return with_variant(plan.variant, [&](auto t) {
     using T = decltype(t);
-    return launch_variant<T::KIND, T::BN, T::BK, T::STAGES, T::CHUNK_KB, T::PAIR>(p, plan.ksplit,
-                                                                                 err, s);
+    return launch_variant<T::KIND, T::BN, T::BK, T::STAGES, T::CHUNK_KB, T::PAIR, T::EPI>(
+        p, plan.ksplit, err, s);
   });
 }
 

@@ -23,8 +23,53 @@ def num_tokens(img_size: int | tuple[int, int]) -> int:
 
 def synthetic_state_dict(seed: int = 0, img_size: int | tuple[int, int] = 224,
                          num_classes: int = 1000, depth: int = 12,
-                         in_chans: int = 3) -> dict[str, torch.Tensor]:
-    """CPU float32 state dict with timm's `vit_base_patch16_*` key names."""
+                         in_chans: int = 3, stats: str = "init") -> dict[str, torch.Tensor]:
+    """CPU float32 state dict with timm's `vit_base_patch16_*` key names.
+
+    stats="init" (default): timm's initialisation, as above. stats="trained":
+    the same draws reshaped to resemble a trained ViT-B/16's statistics (no
+    pretrained checkpoint is available offline): LayerNorm gains spread
+    log-normally and growing with depth, with a few channels per block at
+    5-10; LayerNorm biases N(0, 0.2); linear weights twice as wide, with one
+    entry in a hundred four times larger (heavier row sums); positional and
+    CLS embeddings ten times larger."""
+    if stats not in ("init", "trained"):
+        raise ValueError("stats must be 'init' or 'trained'")
+    sd = _init_state_dict(seed, img_size, num_classes, depth, in_chans)
+    if stats == "trained":
+        _reshape_trained(sd, seed, depth)
+    return sd
+
+
+def _reshape_trained(sd: dict[str, torch.Tensor], seed: int, depth: int) -> None:
+    g = torch.Generator(device="cpu")
+    g.manual_seed(int(seed) + 7919)
+
+    def gains(i):
+        gm = torch.exp(torch.randn(EMBED, generator=g) * (0.3 + 0.05 * i))
+        idx = torch.randperm(EMBED, generator=g)[:4]
+        gm[idx] = 5.0 + 5.0 * torch.rand(4, generator=g)
+        return gm
+
+    def heavy(w):
+        w = w * 2.0
+        mask = torch.rand(w.shape, generator=g) < 0.01
+        return torch.where(mask, w * 4.0, w)
+
+    for i in range(depth):
+        p = f"blocks.{i}."
+        for ln in ("norm1", "norm2"):
+            sd[p + ln + ".weight"] = gains(i)
+            sd[p + ln + ".bias"] = torch.randn(EMBED, generator=g) * 0.2
+        for lin in ("attn.qkv", "attn.proj", "mlp.fc1", "mlp.fc2"):
+            sd[p + lin + ".weight"] = heavy(sd[p + lin + ".weight"])
+    sd["norm.weight"] = gains(depth)
+    sd["norm.bias"] = torch.randn(EMBED, generator=g) * 0.2
+    sd["pos_embed"] = sd["pos_embed"] * 10.0
+    sd["cls_token"] = sd["cls_token"] * 10.0
+
+
+def _init_state_dict(seed, img_size, num_classes, depth, in_chans):
     g = torch.Generator(device="cpu")
     g.manual_seed(int(seed))
     T = num_tokens(img_size)
