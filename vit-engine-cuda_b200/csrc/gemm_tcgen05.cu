@@ -789,8 +789,10 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
             float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[0]);
             epilogue_slab<F16>(args, m_base, lane, n0, part, stg);
           }
+          if (i + 1 < Cfg::kWgSlabs) {
 #pragma unroll
-          for (int c = 0; c + 32 < Cfg::kWgCols; ++c) sum[c] = sum[c + 32];
+            for (int c = 0; c + 32 < Cfg::kWgCols; ++c) sum[c] = sum[c + 32];
+          }
         }
       }
     }
