@@ -327,7 +327,7 @@ typedef struct vitb200_vit_params {
     int num_classes;    /* 1000                                           */
     float ln_eps;       /* 1e-6                                           */
     float attn_scale;   /* 0.125                                          */
-    const float* patch_w_pair; /* TF32 pair of [768][in_chans*256]        */
+    const float* patch_w_pair; /* TF32 pair of [768][in_chans*256], or NULL with patch_w_f16 */
     const float* patch_b;      /* [768]                                   */
     const float* cls_token;    /* [768]                                   */
     const float* pos_embed;    /* [T][768]                                */
@@ -336,6 +336,15 @@ typedef struct vitb200_vit_params {
     const float* norm_b;       /* [768]                                   */
     const float* head_w_pair;  /* TF32 pair of [num_classes][768]         */
     const float* head_b;       /* [num_classes]                           */
+    /* Patch GEMM on FP16 splits instead of the TF32 pair (either may be
+     * NULL, not both; patch_w_f16 wins): the planes [3][768][in_chans*256]
+     * (hi, lo*2^11, hi*2^11) of the weight times a power of two s, and
+     * patch_acc_scale = 2^-11 / s. The pixels are then split to FP16 by the
+     * im2col kernel, so their magnitudes must stay below 32768 (normalised
+     * or 0-255 images do); a larger or non-finite pixel sets the device error
+     * (code 6, vitb200_device_error) instead of failing silently. */
+    const uint16_t* patch_w_f16;
+    float patch_acc_scale;
 } vitb200_vit_params;
 
 /* Workspace needed by vitb200_vit_forward / _features for `batch` images. */

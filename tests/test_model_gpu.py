@@ -248,6 +248,7 @@ def test_operand_choice(case224, cuda):
     splits by default."""
     _, _, _, _, model = case224
     model.prepare()
+    assert model.patch_operands == "f16"
     assert len(model.gemm_operands) == 12
     assert all(k == "f16" for blk in model.gemm_operands for k in blk.values())
 
@@ -257,6 +258,7 @@ def test_tf32_operands_match_oracle(case224, cuda):
     model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()},
                     operands="tf32").to(cuda).eval()
     model.prepare()
+    assert model.patch_operands == "tf32"
     assert all(k == "tf32" for blk in model.gemm_operands for k in blk.values())
     with torch.no_grad():
         out = model(img.to(cuda)).double().cpu()
@@ -420,3 +422,24 @@ def test_trained_like_weights(cuda):
         out = model(img.to(cuda)).double().cpu()
     assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
     assert torch.equal(out.argmax(-1), ref.argmax(-1))
+
+
+def test_out_of_range_pixel_reported(case224, cuda):
+    """The patch GEMM runs on FP16 splits of the pixels, which must stay below
+    32768 in magnitude: a pixel beyond that is reported through the device
+    error word (code 6) rather than producing silent garbage; with
+    operands="tf32" the same image runs on TF32 pairs and matches the oracle."""
+    import vit_cuda
+    state, _, _, _, model = case224
+    img = synthetic_images(1, 224, seed=9)
+    img[0, 1, 100, 37] = 40000.0
+    with torch.no_grad():
+        model(img.to(cuda))
+    assert vit_cuda.device_error(clear=True) == 6
+    m32 = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()},
+                  operands="tf32").to(cuda).eval()
+    with torch.no_grad():
+        out = m32(img.to(cuda)).double().cpu()
+    assert vit_cuda.device_error(clear=True) == 0
+    ref = orc.vit_forward(img, state)
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())

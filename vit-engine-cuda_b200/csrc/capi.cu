@@ -647,9 +647,10 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
     return VITB200_E_INVALID_ARG;
   if (p->img_h < 16 || p->img_w < 16 || p->img_h % 16 || p->img_w % 16)
     return VITB200_E_INVALID_ARG;
-  if (!p->patch_w_pair || !p->patch_b || !p->cls_token || !p->pos_embed || !p->blocks ||
-      !p->norm_w || !p->norm_b)
+  if ((!p->patch_w_pair && !p->patch_w_f16) || !p->patch_b || !p->cls_token || !p->pos_embed ||
+      !p->blocks || !p->norm_w || !p->norm_b)
     return VITB200_E_INVALID_ARG;
+  if (p->patch_w_f16 && !(p->patch_acc_scale > 0.f)) return VITB200_E_INVALID_ARG;
   for (int i = 0; i < p->depth; ++i) {
     const vitb200_block_params& b = p->blocks[i];
     if (!b.norm1_w || !b.norm1_b || !b.qkv_b || !b.proj_b || !b.norm2_w || !b.norm2_b ||
@@ -698,17 +699,28 @@ size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve
   return align_up(c->off, 256);
 }
 
-// patches -> TF32 pair; patch GEMM with bias and positional rows fused into the
-// epilogue (rows b*T+1+p); CLS rows cls + pos[0]. Writes x[B*T][768].
+// patches -> FP16 split (or TF32 pair without FP16 weight planes); patch GEMM
+// with bias and positional rows fused into the epilogue (rows b*T+1+p); CLS
+// rows cls + pos[0]. Writes x[B*T][768].
 int vit_embed(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b,
               const float* img, float* x, int batch, cudaStream_t s) {
   const int D = p->embed_dim;
-  if (int st = im2col_pair_launch(img, batch, p->in_chans, p->img_h, p->img_w, b.pair_a, s,
-                                  p->cls_token, p->pos_embed, x, D))
+  const bool f16 = p->patch_w_f16 != nullptr;
+  uint16_t* a16 = reinterpret_cast<uint16_t*>(b.pair_a);
+  if (int st = im2col_pair_launch(img, batch, p->in_chans, p->img_h, p->img_w,
+                                  f16 ? nullptr : b.pair_a, s, p->cls_token, p->pos_embed, x, D,
+                                  f16 ? a16 : nullptr))
     return st;
   GemmProblem g;
-  g.a_pair = b.pair_a;
-  g.b_pair = p->patch_w_pair;
+  if (f16) {
+    g.f16 = 1;
+    g.a_h16 = a16;
+    g.b_h16 = p->patch_w_f16;
+    g.acc_scale = p->patch_acc_scale;
+  } else {
+    g.a_pair = b.pair_a;
+    g.b_pair = p->patch_w_pair;
+  }
   g.M = d.Mp;
   g.N = D;
   g.Kp = d.Kpatch;

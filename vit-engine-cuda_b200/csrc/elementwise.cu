@@ -389,10 +389,14 @@ int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const floa
 // patches row-major over the (H/16) x (W/16) grid, as the reference kernel
 // csrc/kernels/patch_embed.cu:29-44 and torch's Conv2d weight layout agree.
 // With x != null it also writes each image's CLS row of the token matrix,
-// x[b][0] = cls + pos[0] (the patch GEMM's epilogue writes rows 1..P).
+// x[b][0] = cls + pos[0] (the patch GEMM's epilogue writes rows 1..P). With
+// h16 != null the patches are written as FP16 splits instead (planes
+// h16[2][B*P][C*256]: hi, lo*2^11; a magnitude reaching the split's limit
+// sets the device error).
 __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, int H, int W,
                                    float* __restrict__ pair, const float* __restrict__ cls,
-                                   const float* __restrict__ pos, float* __restrict__ x, int E) {
+                                   const float* __restrict__ pos, float* __restrict__ x, int E,
+                                   uint16_t* __restrict__ h16, int* err) {
   griddep_wait();
   griddep_launch_dependents();
   const int gw = W / 16, gh = H / 16;
@@ -413,14 +417,25 @@ __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, 
     const float* src = img + ((b * C + c) * H + gy * 16 + py) * static_cast<int64_t>(W) +
                        gx * 16 + px;
     const float4 v = __ldcs(reinterpret_cast<const float4*>(src));
-    float4 h, l;
-    tf32_split(v.x, h.x, l.x);
-    tf32_split(v.y, h.y, l.y);
-    tf32_split(v.z, h.z, l.z);
-    tf32_split(v.w, h.w, l.w);
-    float* dst = pair + m * K + k;
-    *reinterpret_cast<float4*>(dst) = h;
-    *reinterpret_cast<float4*>(dst + plane) = l;
+    if (h16 != nullptr) {
+      uint32_t h0, l0, h1, l1;
+      h16_split2(v.x, v.y, h0, l0);
+      h16_split2(v.z, v.w, h1, l1);
+      const float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      if (!(mx < kH16Limit)) report_error(err, kErrF16Range);
+      uint16_t* dst = h16 + m * K + k;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(dst + plane) = make_uint2(l0, l1);
+    } else {
+      float4 h, l;
+      tf32_split(v.x, h.x, l.x);
+      tf32_split(v.y, h.y, l.y);
+      tf32_split(v.z, h.z, l.z);
+      tf32_split(v.w, h.w, l.w);
+      float* dst = pair + m * K + k;
+      *reinterpret_cast<float4*>(dst) = h;
+      *reinterpret_cast<float4*>(dst + plane) = l;
+    }
     (void)gh;
   }
   if (x != nullptr) {
@@ -435,16 +450,20 @@ __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, 
 }
 
 int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair,
-                       cudaStream_t s, const float* cls, const float* pos, float* x, int E) {
-  if (B < 0 || C <= 0 || H <= 0 || W <= 0 || H % 16 || W % 16 || !img || !pair ||
+                       cudaStream_t s, const float* cls, const float* pos, float* x, int E,
+                       uint16_t* h16) {
+  if (B < 0 || C <= 0 || H <= 0 || W <= 0 || H % 16 || W % 16 || !img || (!pair && !h16) ||
       (x && (!cls || !pos || E <= 0)))
     return VITB200_E_INVALID_ARG;
-  if (reinterpret_cast<uintptr_t>(img) % 16 || reinterpret_cast<uintptr_t>(pair) % 16)
+  if (reinterpret_cast<uintptr_t>(img) % 16 || reinterpret_cast<uintptr_t>(pair) % 16 ||
+      reinterpret_cast<uintptr_t>(h16) % 16)
     return VITB200_E_ALIGNMENT;
   if (B == 0) return 0;
+  int* err = device_error_word();
+  if (err == nullptr) return VITB200_E_INVALID_ARG;
   const int64_t work = static_cast<int64_t>(B) * (H / 16) * (W / 16) * C * 64;
   if (int st_ = launch_kernel(im2col_pair_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, 1,
-      img, B, C, H, W, pair, cls, pos, x, E))
+      img, B, C, H, W, pair, cls, pos, x, E, h16, err))
     return st_;
   return cuda_status(cudaGetLastError());
 }

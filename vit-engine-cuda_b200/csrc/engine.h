@@ -122,11 +122,12 @@ int layernorm_launch(const float* x, int64_t ldx, const float* gamma, const floa
 int cls_head_launch(const float* x, int64_t cls_stride, const float* gamma, const float* beta,
                     float eps, const float* w_pair, const float* bias, int C, int E, int batch,
                     float* logits, float* features, cudaStream_t s);
-// im2col into the TF32 pair; with x, also the CLS rows x[b][0] = cls + pos[0]
-// of the [B][P+1][E] token matrix.
+// im2col into the TF32 pair (or, with h16, the FP16 split [2][B*P][C*256]);
+// with x, also the CLS rows x[b][0] = cls + pos[0] of the [B][P+1][E] token
+// matrix.
 int im2col_pair_launch(const float* img, int B, int C, int H, int W, float* pair, cudaStream_t s,
                        const float* cls = nullptr, const float* pos = nullptr,
-                       float* x = nullptr, int E = 0);
+                       float* x = nullptr, int E = 0, uint16_t* h16 = nullptr);
 int cls_pos_launch(const float* cls, int64_t cls_stride, const float* pos, const float* patches,
                    float* out, int B, int P, int E, cudaStream_t s);
 int gemm_k0_launch(const GemmProblem& p, cudaStream_t s);

@@ -354,6 +354,64 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
     return;
   }
 
+  if (e.mode == kModePatch && full && e.out && a.vec_out && !e.out_pair && !e.out_h16 &&
+      !e.residual && N % 4 == 0 && reinterpret_cast<uintptr_t>(e.pos) % 16 == 0) {
+    // Patch rows through the transpose buffer: each row's positional row is
+    // added, and row m = b * P + p is stored as token row b * T + 1 + p.
+    const int rsub = lane >> 3;
+    const int q = lane & 7;
+    const int c4 = q * 4;
+    // (image, patch) of this lane's rows m_base + rsub + 4k, stepped without
+    // a division per row.
+    const int64_t m0 = m_base + rsub;
+    const int64_t b0 = m0 / e.P;
+    const int p0 = static_cast<int>(m0 - b0 * e.P);
+    int64_t bk = b0;
+    int pk = p0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + rsub;
+      const int64_t mr = m_base + r;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (mr < a.M)
+        t = *reinterpret_cast<const float4*>(e.pos + static_cast<int64_t>(1 + pk) * N +
+                                              col_base + c4);
+      *reinterpret_cast<float4*>(stg + stg_at(r, q)) = t;
+      pk += 4;
+      while (pk >= e.P) {
+        pk -= e.P;
+        ++bk;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(stg + stg_at(lane, j / 4));
+      *reinterpret_cast<float4*>(stg + stg_at(lane, j / 4)) =
+          make_float4(v[j] + t.x, v[j + 1] + t.y, v[j + 2] + t.z, v[j + 3] + t.w);
+    }
+    __syncwarp();
+    bk = b0;
+    pk = p0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + rsub;
+      const int64_t mr = m_base + r;
+      const float4 t = *reinterpret_cast<const float4*>(stg + stg_at(r, q));
+      if (mr < a.M) {
+        const int64_t orow = bk * e.T + 1 + pk;
+        *reinterpret_cast<float4*>(e.out + orow * e.ldo + col_base + c4) = t;
+      }
+      pk += 4;
+      while (pk >= e.P) {
+        pk -= e.P;
+        ++bk;
+      }
+    }
+    __syncwarp();
+    return;
+  }
+
   // Generic path (partial slab, positional rows, unaligned outputs): per row.
   if (!row_ok) return;
   int64_t out_row = m;

@@ -59,6 +59,7 @@ class VitParams(ctypes.Structure):
         ("pos_embed", c_void_p), ("blocks", POINTER(BlockParams)),
         ("norm_w", c_void_p), ("norm_b", c_void_p),
         ("head_w_pair", c_void_p), ("head_b", c_void_p),
+        ("patch_w_f16", c_void_p), ("patch_acc_scale", c_float),
     ]
 
 

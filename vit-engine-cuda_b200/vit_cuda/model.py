@@ -132,13 +132,22 @@ class ViTCUDA(nn.Module):
 
     def _compute_splits(self) -> tuple[dict, dict]:
         """The split weights on the model's device: tensors named
-        ``patch.pair``, ``head.pair`` and per block ``blocks.{i}.{gemm}.pair``
-        (TF32 pair) or ``blocks.{i}.{gemm}.f16`` (FP16 planes), plus string
-        metadata: ``blocks.{i}.{gemm}`` = "f16" | "tf32", the FP16 GEMMs'
-        ``.acc_scale`` and ``blocks.{i}.attn`` = "f16" | "tf32"."""
-        tensors = {"patch.pair": _split_pair(self.patch_weight),
-                   "head.pair": _split_pair(self.head_weight)}
+        ``patch.f16`` (FP16 planes) or ``patch.pair``, ``head.pair`` and per
+        block ``blocks.{i}.{gemm}.pair`` (TF32 pair) or ``blocks.{i}.{gemm}.f16``
+        (FP16 planes), plus string metadata: ``patch`` and ``blocks.{i}.{gemm}``
+        = "f16" | "tf32", the FP16 GEMMs' ``.acc_scale`` and ``blocks.{i}.attn``
+        = "f16" | "tf32". The patch GEMM's input is the image itself, whose
+        pixels the FP16 path requires below 32768 in magnitude (the im2col
+        kernel reports larger ones through the device error)."""
+        tensors = {"head.pair": _split_pair(self.head_weight)}
         meta = {}
+        pw = self.patch_weight.reshape(self.patch_weight.shape[0], -1).contiguous()
+        if self.operands == "auto" and f16_weight_ok(pw):
+            tensors["patch.f16"], acc_scale = f16_weight(pw)
+            meta["patch"], meta["patch.acc_scale"] = "f16", repr(acc_scale)
+        else:
+            tensors["patch.pair"] = _split_pair(self.patch_weight)
+            meta["patch"] = "tf32"
         for i, blk in enumerate(self.blocks):
             bounds = block_input_bounds(blk, 768)
             for name in ("qkv", "proj", "fc1", "fc2"):
@@ -187,7 +196,7 @@ class ViTCUDA(nn.Module):
         with torch.cuda.device(self.patch_weight.device):
             _lib.check(lib.vitb200_init(), "vitb200_init")
             imported = getattr(self, "_imported", None)
-            if imported is not None and imported[0]["patch.pair"].device == self.patch_weight.device:
+            if imported is not None and imported[0]["head.pair"].device == self.patch_weight.device:
                 splits, meta = imported
             else:
                 splits, meta = self._compute_splits()
@@ -228,12 +237,16 @@ class ViTCUDA(nn.Module):
                 mlp_dim=self.blocks[0].fc1_weight.shape[0], patch=16, in_chans=self.in_chans,
                 img_h=self.img_size[0], img_w=self.img_size[1], num_classes=self.num_classes,
                 ln_eps=self.eps, attn_scale=self.scale,
-                patch_w_pair=splits["patch.pair"].data_ptr(),
+                patch_w_pair=ptr(splits.get("patch.pair")),
                 patch_b=vecs["patch_bias"].data_ptr(),
                 cls_token=vecs["cls_token"].data_ptr(), pos_embed=vecs["pos_embed"].data_ptr(),
                 blocks=ctypes.cast(blocks, ctypes.POINTER(BlockParams)),
                 norm_w=vecs["norm_gamma"].data_ptr(), norm_b=vecs["norm_beta"].data_ptr(),
-                head_w_pair=splits["head.pair"].data_ptr(), head_b=vecs["head_bias"].data_ptr())
+                head_w_pair=splits["head.pair"].data_ptr(), head_b=vecs["head_bias"].data_ptr(),
+                patch_w_f16=ptr(splits.get("patch.f16")),
+                patch_acc_scale=(float(meta["patch.acc_scale"])
+                                 if meta.get("patch", "tf32") == "f16" else 0.0))
+            self.patch_operands = meta.get("patch", "tf32")
             if self.head_weight.shape[0] != self.num_classes:
                 raise RuntimeError("head weight rows must equal num_classes")
         self._prepared = (key, splits, params, blocks, keep, meta)
