@@ -799,19 +799,29 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       if constexpr (!PAIR) {
         if (ksplit > 1) {
           // Split K over a cluster of ksplit CTAs, one work unit each (split =
-          // cluster rank). The others leave their partial sums in their own
-          // stage ring, idle now that their last MMA has completed; the leader
-          // (split 0) adds them in split order over distributed shared memory
-          // (deterministic) and finishes the tile. Layout [warp][c / 4][lane]
-          // of float4: each warp access is 512 contiguous bytes.
+          // cluster rank). Each warp slab (this warp's 32 rows x kWgCols
+          // columns) is finished by one CTA of the cluster, `owner`, so that
+          // the reduction and the epilogue are shared out: the other CTAs leave
+          // their partial sums of it in their own stage ring, idle now that
+          // their last MMA has completed, and the owner adds all partials in
+          // split order over distributed shared memory (deterministic, the
+          // same order whichever CTA adds). Layout [warp][c / 4][lane] of
+          // float4: each warp access is 512 contiguous bytes.
           const int slab = warp - 4;
+          const int owner = slab % ksplit;
           float4* part = reinterpret_cast<float4*>(ring) + slab * (Cfg::kWgCols / 4) * 32 + lane;
-          if (split != 0) {
+          // Split 0 keeps its partial in registers when it owns the slab;
+          // every other partial is published (an owner other than split 0
+          // reads its own back in its place in the order).
+          if (split != 0 || owner != 0) {
             fence_proxy_async_smem();
 #pragma unroll
             for (int c = 0; c < Cfg::kWgCols; c += 4)
               part[(c / 4) * 32] = make_float4(sum[c], sum[c + 1], sum[c + 2], sum[c + 3]);
-            mbar_arrive_cluster(mapa_shared(smem_addr(&split_bar[slab]), 0));
+          }
+          if (split != owner) {
+            mbar_arrive_cluster(
+                mapa_shared(smem_addr(&split_bar[slab]), static_cast<uint32_t>(owner)));
             continue;
           }
           const bool got = mbar_wait_acq_cluster(&split_bar[slab], 0, err, kErrWaitSplit);
@@ -819,7 +829,19 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
             ok = false;
             break;
           }
+          // sum = p_0 + p_1 + ... in split order.
           const uint32_t part_addr = smem_addr(part);
+          if (split != 0) {
+            const uint32_t src = mapa_shared(part_addr, 0u);
+#pragma unroll
+            for (int c = 0; c < Cfg::kWgCols; c += 4) {
+              const float4 t = ld_shared_cluster_f4(src + static_cast<uint32_t>(c / 4) * 512u);
+              sum[c] = t.x;
+              sum[c + 1] = t.y;
+              sum[c + 2] = t.z;
+              sum[c + 3] = t.w;
+            }
+          }
           for (int sp = 1; sp < ksplit; ++sp) {
             const uint32_t src = mapa_shared(part_addr, static_cast<uint32_t>(sp));
 #pragma unroll
