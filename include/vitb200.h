@@ -71,7 +71,7 @@ int vitb200_device_error(int* code, int clear);
 
 /* Failure-reporting check: launches a kernel whose bounded wait is never
  * satisfied (kind 0: the GEMM / attention pipeline wait, which reports code
- * 1; kind 1: the split-K leader's cluster-scope wait, code 7). After the wait
+ * 1; kind 1: a split-K owner's cluster-scope wait, code 7). After the wait
  * limit (1 s) it records the code in the device error word and returns; the
  * context stays usable. No counterpart in the reference (its kernels have no
  * waits). */
@@ -102,10 +102,10 @@ int vitb200_set_gemm_variant(int variant);
 /* Split-K of small single-CTA GEMM launches (on by default). When the output
  * tile grid fills at most half the SMs (e.g. the block GEMMs of a batch-1
  * forward, M = 197 rows), the launch splits K into d <= 8 equal parts over a
- * thread-block cluster of d CTAs per tile; the other CTAs leave their fp32
- * partial tiles in their shared memory and the cluster's first CTA adds them
- * in split order over distributed shared memory (deterministic) and writes the
- * tile. An image's logits are bitwise identical in any batch of at least 7
+ * thread-block cluster of d CTAs per tile; each CTA keeps its fp32 partial
+ * tile in its shared memory, and the tile's 32 x 32 slabs are shared out among
+ * the cluster's CTAs, each adding the partials of its slabs in split order
+ * over distributed shared memory (deterministic) and writing them. An image's logits are bitwise identical in any batch of at least 7
  * images at 224x224 (CTA-pair tiles from 1024 token rows, no split); with
  * split-K off also among batches of up to 5 images; otherwise they agree to
  * FP32 rounding. No counterpart in the reference (one CTA per 32x32 output
@@ -113,6 +113,14 @@ int vitb200_set_gemm_variant(int variant);
  * keeps the setting it was captured with). Returns the previous setting;
  * process-wide. */
 int vitb200_set_split_k(int enable);
+
+/* Forces the K split of later small single-CTA GEMM launches (those split-K
+ * applies to) to ksplit CTAs per tile wherever that split fits (ksplit divides
+ * the K blocks, the CTAs fit in one wave and the clusters are co-resident);
+ * 0 restores the automatic choice, values outside 0..8 are ignored. No effect
+ * while split-K is off. Returns the previous setting. For tuning and tests;
+ * process-wide. */
+int vitb200_set_gemm_split(int ksplit);
 
 /* The tile configuration (*variant, as in vitb200_set_gemm_variant) and the K
  * split (*ksplit, 1 = none) that a GEMM of M x K by K x N (f16 = 1: FP16-split

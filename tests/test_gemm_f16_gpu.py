@@ -206,3 +206,40 @@ def test_large_launches_do_not_split(vlib, cuda):
             v, d = vlib.gemm_plan(50432, k, n, f16)
             assert d == 1 and v == (15 if f16 else 6)
         assert vlib.gemm_plan(1024, 768, 768, f16)[1] == 1
+
+
+@pytest.mark.parametrize("kind", ["f16", "tf32"])
+@pytest.mark.parametrize("epi", ["bias", "gelu", "resid"])
+def test_forced_split_k_every_d(vlib, cuda, kind, epi):
+    """Every K split d = 2..8 (vitb200_set_gemm_split), including those for
+    which the tile's eight warp slabs are shared out unevenly among the
+    cluster's CTAs (d = 3, 5, 6, 7): FP32 parity, bitwise repeatable, and a
+    different summation from the unsplit launch (the split ran). K = 64 * 840
+    K blocks divide by every d; 4 output tiles keep d CTAs each in one wave."""
+    torch.manual_seed(11)
+    m, k, n = 197, 64 * 840, 128
+    x = torch.randn(m, k, device=cuda)
+    w = torch.randn(n, k, device=cuda) * 0.05
+    bias = torch.randn(n, device=cuda)
+    res = torch.randn(m, n, device=cuda) if epi == "resid" else None
+
+    def run():
+        if kind == "f16":
+            return run_f16(vlib, x, w, bias, res, epi)
+        return run_gemm(vlib, x, w, bias, res, epi)
+
+    old = vlib.lib.vitb200_set_gemm_split(1)
+    try:
+        assert vlib.gemm_plan(m, k, n, kind == "f16")[1] == 1
+        y0 = run()
+        for d in range(2, 9):
+            vlib.lib.vitb200_set_gemm_split(d)
+            assert vlib.gemm_plan(m, k, n, kind == "f16")[1] == d
+            y1, y2 = run(), run()
+            assert torch.equal(y1, y2), d
+            assert not torch.equal(y0, y1), d
+            check_fp32_parity(y1, x, w, bias, res, epi)
+    finally:
+        vlib.lib.vitb200_set_gemm_split(old)
+    assert old == 0
+    assert vlib.device_error(clear=True) == 0

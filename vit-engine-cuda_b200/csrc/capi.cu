@@ -175,6 +175,8 @@ int vitb200_set_gemm_variant(int variant) { return gemm_set_variant(variant); }
 
 int vitb200_set_split_k(int enable) { return gemm_set_split_k(enable); }
 
+int vitb200_set_gemm_split(int ksplit) { return gemm_set_split(ksplit); }
+
 int vitb200_check_wait_timeout(int kind, void* stream) {
   VITB200_GUARD_BEGIN
   if (kind != 0 && kind != 1) return VITB200_E_INVALID_ARG;

@@ -22,7 +22,7 @@ enum DeviceError : int {
   kErrWaitAccEmpty = 4, // MMA issuer waited too long for a drained accumulator
   kErrDrain = 5,        // error path: in-flight copies did not land in time
   kErrF16Range = 6,     // a value outside the FP16-split range reached a split
-  kErrWaitSplit = 7,    // split-K leader waited too long for the other CTAs' partial sums
+  kErrWaitSplit = 7,    // split-K owner waited too long for the other CTAs' partial sums
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 1000000000ull;  // 1 s

@@ -90,11 +90,14 @@ int gemm_prepare_device();
 // Forces one tile configuration (0 = automatic choice); returns the old value.
 int gemm_set_variant(int v);
 // Launches a kernel whose bounded wait never completes (kind 0: a pipeline
-// wait, error code 1; 1: the split-K leader's cluster-scope wait, code 7).
+// wait, error code 1; 1: a split-K owner's cluster-scope wait, code 7).
 int wait_timeout_launch(int kind, cudaStream_t s);
 // Switches split-K of later small single-CTA launches on / off; returns the
 // old setting.
 int gemm_set_split_k(int enable);
+// Forces the K split of later small single-CTA launches to d where it fits
+// (0 = automatic choice); returns the old value.
+int gemm_set_split(int d);
 // Tile configuration (variant) and K split a launch of this shape would use
 // on the current device.
 int gemm_plan(int64_t M, int N, int Kp, int f16, int* variant, int* ksplit);

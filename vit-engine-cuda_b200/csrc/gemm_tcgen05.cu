@@ -980,8 +980,10 @@ constexpr int kF16PairVariant = 15;
 // Process-wide switches and per-device caches; atomic, since host threads
 // (one per GPU, say) may launch concurrently.
 std::atomic<int> g_forced_variant{0};
-// Split-K of small single-CTA launches (on unless switched off).
+// Split-K of small single-CTA launches (on unless switched off), and a forced
+// split (0 = the cost model's choice).
 std::atomic<int> g_split_k{1};
+std::atomic<int> g_forced_split{0};
 
 // Cluster-of-two slots that fit on the device at once, per device (0 = not
 // queried yet).
@@ -1192,7 +1194,9 @@ GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   const int cands_f16[2] = {10, 11}, cands_tf32[2] = {1, 3};  // BN = 128, 64
   const int* cands = f16 ? cands_f16 : cands_tf32;
-  int64_t best_cost = -1;
+  int64_t best_cost = 0;
+  bool have = false;
+  const int forced_d = g_split_k ? g_forced_split.load() : 0;
   for (int i = 0; i < (use_forced ? 1 : 2); ++i) {
     const int v = use_forced ? forced : cands[i];
     with_variant(v, [&](auto t) {
@@ -1206,10 +1210,12 @@ GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
                         d))
           continue;
         const int64_t waves = (tiles * d + sms - 1) / sms;
-        const int64_t cost =
-            waves * (num_kb / d) * (T::Cfg::kStageBytes / T::STAGES) +
-            (d > 1 ? kSplitFixedCost + (d - 1) * kSplitPerCtaCost : 0);
-        if (best_cost < 0 || cost < best_cost) {
+        int64_t cost = waves * (num_kb / d) * (T::Cfg::kStageBytes / T::STAGES) +
+                       (d > 1 ? kSplitFixedCost + (d - 1) * kSplitPerCtaCost : 0);
+        // A forced split that fits wins over every other choice.
+        if (forced_d > 0 && d == forced_d) cost -= int64_t{1} << 40;
+        if (!have || cost < best_cost) {
+          have = true;
           best_cost = cost;
           plan.variant = v;
           plan.ksplit = d;
@@ -1225,6 +1231,12 @@ GemmPlan plan_gemm(int64_t M, int N, int Kp, bool f16) {
 
 int gemm_set_split_k(int enable) {
   const int old = g_split_k.exchange(enable != 0 ? 1 : 0);
+  return old;
+}
+
+int gemm_set_split(int d) {
+  const int old = g_forced_split.load();
+  if (d >= 0 && d <= kMaxSplit) g_forced_split.store(d);
   return old;
 }
 

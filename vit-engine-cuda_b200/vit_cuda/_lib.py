@@ -73,6 +73,7 @@ _SIGNATURES = {
     "vitb200_launch_count": (ctypes.c_uint64, []),
     "vitb200_set_gemm_variant": (c_int, [c_int]),
     "vitb200_set_split_k": (c_int, [c_int]),
+    "vitb200_set_gemm_split": (c_int, [c_int]),
     "vitb200_check_wait_timeout": (c_int, [c_int, _P]),
     "vitb200_gemm_plan": (c_int, [c_int64, c_int, c_int, c_int, POINTER(c_int), POINTER(c_int)]),
     "vitb200_split_tf32": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int, _P]),
@@ -193,6 +194,13 @@ def set_split_k(enabled: bool) -> bool:
     agree to FP32 rounding. Affects later launches (not a captured graph).
     Returns the previous setting; process-wide."""
     return bool(lib.vitb200_set_split_k(1 if enabled else 0))
+
+
+def set_gemm_split(ksplit: int) -> int:
+    """Forces the K split of later small GEMM launches to `ksplit` wherever it
+    fits (0: the automatic choice). For tuning and tests; returns the previous
+    setting; process-wide."""
+    return int(lib.vitb200_set_gemm_split(int(ksplit)))
 
 
 def gemm_plan(M: int, K: int, N: int, f16: bool) -> tuple[int, int]:
