@@ -43,6 +43,8 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -67,6 +69,10 @@ struct GemmArgs {
   int vec_h16;     // FP16-pair rows are 16-byte aligned
   int vec_bias;    // bias is 16-byte aligned
   float acc_scale; // F16 kernels: multiplies the accumulator (a power of two)
+  int tma_h16;     // FP16 splits of the result go out through tmap_h (TMA stores):
+                   // out_h16 (planes 0-1), or q16 | k16 (planes 0-1 | 2-3)
+  int tma_out;     // the fp32 result goes out through tmap_h (TMA stores), and the
+                   // residual (the same tensor) comes in through it (TMA loads)
   int* err;
   GemmEpilogue epi;
 };
@@ -189,9 +195,43 @@ __device__ __forceinline__ void h16_slab_store(const float (&v)[32], float* stg,
   __syncwarp();
 }
 
+// The same split through a TMA tensor store: the warp writes its slab into
+// its 4 KB transpose buffer in the layout of the map's box {32 columns, 32
+// rows, 2 planes} with the 64-byte swizzle (16-byte chunk q of row r at
+// chunk q ^ ((r >> 1) & 3): conflict-free), and lane 0 stores it. Before the
+// buffer is written again lane 0 waits until the previous store has read it;
+// rows past M are clipped by the map.
+__device__ __forceinline__ void h16_slab_store_tma(const float (&v)[32], float* stg, int lane,
+                                                   int64_t m_base, int64_t col_base,
+                                                   const CUtensorMap* tmap_h, int plane0) {
+  uint8_t* buf = reinterpret_cast<uint8_t*>(stg);
+  if (lane == 0) bulk_wait_group_read<0>();
+  __syncwarp();
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) h16_split2(v[8 * q + 2 * t], v[8 * q + 2 * t + 1], hw[t], lw[t]);
+    const int at = lane * 64 + 16 * (q ^ sw);
+    *reinterpret_cast<uint4*>(buf + at) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(buf + 2048 + at) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(tmap_h, buf, static_cast<int>(col_base), static_cast<int>(m_base), plane0);
+    bulk_commit_group();
+  }
+}
+
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err);
+
 template <bool F16>
 __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base, int lane, int n0,
-                                              float (&v)[32], float* stg) {
+                                              float (&v)[32], float* stg,
+                                              const CUtensorMap* tmap_h, uint64_t* res_bar,
+                                              uint32_t& res_phase) {
   const GemmEpilogue& e = a.epi;
   const int N = a.N;
   const int64_t m = m_base + lane;
@@ -235,8 +275,11 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = v[j] * sc;  // exact: a power of two
     if (part < 2) {
-      h16_slab_store(v, stg, lane, m_base, a.M, part == 0 ? e.q16 : e.k16, E, a.M * E,
-                     n0 - part * E);
+      if (a.tma_h16)  // q and k: planes 0-1 and 2-3 of one map
+        h16_slab_store_tma(v, stg, lane, m_base, n0 - part * E, tmap_h, 2 * part);
+      else
+        h16_slab_store(v, stg, lane, m_base, a.M, part == 0 ? e.q16 : e.k16, E, a.M * E,
+                       n0 - part * E);
       return;
     }
     // V: transposed per (image, head); lanes hold consecutive tokens, so each
@@ -292,14 +335,36 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
     const int rsub = lane >> 3;        // row within a group of four
     const int q = lane & 7;            // this lane's 16-byte chunk of a 32-column row
     const int c4 = q * 4;
+    // TMA path: the buffer's layout (chunk q of row r at q ^ (r & 7)) is the
+    // map's 128-byte swizzle of the box {32 columns, 32 rows}. Before it is
+    // written again, the previous slab's store must have read it.
+    if (a.tma_out) {
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+    }
     if (e.residual != nullptr) {
+      if (a.tma_out) {
+        // The residual slab (rows past M read as zeros) in one load.
+        if (lane == 0) {
+          mbar_arrive_expect_tx(res_bar, 32 * 32 * 4);
+          tma_load_3d(stg, tmap_h, res_bar, static_cast<int>(col_base), static_cast<int>(m_base),
+                      0);
+        }
+        // Every lane waits (acquire) before reading the slab; a wait that
+        // gives up records its code and lets the copy land before going on.
+        if (!mbar_wait(res_bar, res_phase, a.err, kErrWaitFull))
+          drain_wait(res_bar, res_phase, a.err);
+        res_phase ^= 1u;
+      } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = 4 * k + rsub;
-        const int64_t mr = m_base + r;
-        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (mr < a.M) t = *reinterpret_cast<const float4*>(e.residual + mr * e.ldr + col_base + c4);
-        *reinterpret_cast<float4*>(stg + stg_at(r, q)) = t;
+        for (int k = 0; k < 8; ++k) {
+          const int r = 4 * k + rsub;
+          const int64_t mr = m_base + r;
+          float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (mr < a.M)
+            t = *reinterpret_cast<const float4*>(e.residual + mr * e.ldr + col_base + c4);
+          *reinterpret_cast<float4*>(stg + stg_at(r, q)) = t;
+        }
       }
       __syncwarp();
 #pragma unroll
@@ -328,7 +393,16 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4*>(stg + stg_at(lane, j / 4)) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-      flush(e.out + plane_off, e.ldo);
+      if (a.tma_out) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(tmap_h, stg, static_cast<int>(col_base), static_cast<int>(m_base), 0);
+          bulk_commit_group();
+        }
+      } else {
+        flush(e.out + plane_off, e.ldo);
+      }
     }
     if (e.out_pair != nullptr) {
 #pragma unroll
@@ -349,8 +423,12 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
       }
       flush(e.out_pair + e.pair_plane, e.ldp);
     }
-    if (e.out_h16 != nullptr)
-      h16_slab_store(v, stg, lane, m_base, a.M, e.out_h16, e.ldh, e.h16_plane, col_base);
+    if (e.out_h16 != nullptr) {
+      if (a.tma_h16)
+        h16_slab_store_tma(v, stg, lane, m_base, col_base, tmap_h, 0);
+      else
+        h16_slab_store(v, stg, lane, m_base, a.M, e.out_h16, e.ldh, e.h16_plane, col_base);
+    }
     return;
   }
 
@@ -503,7 +581,8 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
 template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI>
 __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                       const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
+                       const __grid_constant__ CUtensorMap tmap_b,
+                       const __grid_constant__ CUtensorMap tmap_h, const GemmArgs args) {
   using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
   using Epi = EpiCfg<EPI>;
   constexpr bool F16 = Cfg::F16;
@@ -514,6 +593,7 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
   __shared__ __align__(8) uint64_t chunk_empty_bar[Cfg::kNumBufs];
   __shared__ __align__(8) uint64_t mma_done_bar;
   __shared__ __align__(8) uint64_t split_bar[4 * EPI];  // split-K: other CTAs' partials ready
+  __shared__ __align__(8) uint64_t res_bar[4 * EPI];    // per epilogue warp: residual slab landed
   __shared__ uint32_t tmem_base_slot;
 
   const int warp = threadIdx.x >> 5;
@@ -540,6 +620,7 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       mbar_init(&chunk_empty_bar[b], (PAIR ? 2 : 1) * 4 * EPI);
     }
     mbar_init(&mma_done_bar, 1);
+    for (int i = 0; i < 4 * EPI; ++i) mbar_init(&res_bar[i], 1);
     if (!PAIR && args.ksplit > 1) {
       // one arrival per lane of each other CTA's slab warp
       for (int i = 0; i < 4 * EPI; ++i) mbar_init(&split_bar[i], 32 * (args.ksplit - 1));
@@ -751,6 +832,7 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     float* stg = reinterpret_cast<float*>(ring + STAGES * Cfg::kStageBytes) +
                  (warp - 4) * kStgWords;
+    uint32_t res_phase = 0;  // parity of this warp's next residual load (TMA path)
     int local = 0;
     bool ok = true;
     for (int w = unit; w < num_work && ok; w += num_units, ++local) {
@@ -867,7 +949,8 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
           const int n0 = n_blk * BN + slab * 32;
           if ((Cfg::kSlabs % EPI == 0 || slab < Cfg::kSlabs) && n0 < args.N) {
             float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[0]);
-            epilogue_slab<F16>(args, m_base, lane, n0, part, stg);
+            epilogue_slab<F16>(args, m_base, lane, n0, part, stg, &tmap_h, &res_bar[warp - 4],
+                               res_phase);
           }
           if (i + 1 < Cfg::kWgSlabs) {
 #pragma unroll
@@ -876,6 +959,8 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
         }
       }
     }
+    // TMA stores of the result complete before the CTA can exit.
+    if ((args.tma_h16 || args.tma_out) && lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -980,6 +1065,14 @@ constexpr int kF16PairVariant = 15;
 // Process-wide switches and per-device caches; atomic, since host threads
 // (one per GPU, say) may launch concurrently.
 std::atomic<int> g_forced_variant{0};
+bool tma_store_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VITB200_TMA_STORE");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 // Split-K of small single-CTA launches (on unless switched off), and a forced
 // split (0 = the cost model's choice).
 std::atomic<int> g_split_k{1};
@@ -1079,6 +1172,42 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
   a.vec_bias = (e.bias != nullptr) && (reinterpret_cast<uintptr_t>(e.bias) % 16 == 0);
   a.err = err;
   a.epi = e;
+  // FP16 splits written through TMA tensor stores from the transpose buffers
+  // (box {32 columns, 32 rows, 2 planes}, 64-byte swizzle): the split as the
+  // only output (fc1's H), and the q and k splits of the QKV epilogue when k16
+  // directly follows q16's two planes.
+  CUtensorMap th;
+  std::memset(&th, 0, sizeof(th));
+  a.tma_h16 = 0;
+  a.tma_out = 0;
+  if (tma_store_enabled()) {
+    const uint32_t box[3] = {32, 32, 2};
+    if (e.out_h16 != nullptr && a.vec_h16 && e.out == nullptr && e.out_pair == nullptr &&
+        e.residual == nullptr && e.mode == kModePlain && p.N % 32 == 0) {
+      const uint64_t dims[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), 2};
+      const uint64_t strides[2] = {static_cast<uint64_t>(e.ldh) * 2,
+                                   static_cast<uint64_t>(e.h16_plane) * 2};
+      if (int st2 = encode_tmap_typed(&th, 3, e.out_h16, dims, strides, box, 0, 1)) return st2;
+      a.tma_h16 = 1;
+    } else if (e.mode == kModeQKVAttn16 && e.k16 == e.q16 + 2 * p.M * e.e_split) {
+      const uint64_t E = static_cast<uint64_t>(e.e_split);
+      const uint64_t dims[3] = {E, static_cast<uint64_t>(p.M), 4};
+      const uint64_t strides[2] = {E * 2, static_cast<uint64_t>(p.M) * E * 2};
+      if (int st2 = encode_tmap_typed(&th, 3, e.q16, dims, strides, box, 0, 1)) return st2;
+      a.tma_h16 = 1;
+    } else if (e.out != nullptr && a.vec_out && e.out_pair == nullptr && e.out_h16 == nullptr &&
+               e.mode == kModePlain && p.N % 32 == 0 &&
+               (e.residual == nullptr || (e.residual == e.out && e.ldr == e.ldo))) {
+      // The fp32 result (and the residual it replaces), box {32 columns, 32
+      // rows}: the transpose buffer's layout is the map's 128-byte swizzle.
+      const uint64_t dims[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), 1};
+      const uint64_t strides[2] = {static_cast<uint64_t>(e.ldo) * 4,
+                                   static_cast<uint64_t>(e.ldo) * 4 * static_cast<uint64_t>(p.M)};
+      const uint32_t box32[3] = {32, 32, 1};
+      if (int st2 = encode_tmap_typed(&th, 3, e.out, dims, strides, box32, 1, 0)) return st2;
+      a.tma_out = 1;
+    }
+  }
   if constexpr (PAIR) {
     int dev = 0;
     if (int st2 = cuda_status(cudaGetDevice(&dev))) return st2;
@@ -1106,7 +1235,7 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
     }
     const dim3 grid(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
     st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
-                       dim3(kThreads), Cfg::kSmemBytes, s, 2, ta, tb, a);
+                       dim3(kThreads), Cfg::kSmemBytes, s, 2, ta, tb, th, a);
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
@@ -1115,7 +1244,7 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
         a.ksplit > 1 ? tiles * a.ksplit : std::min<int64_t>(tiles, device_num_sms())));
     st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
                        dim3(kThreads), Cfg::kSmemBytes, s, static_cast<unsigned>(a.ksplit), ta,
-                       tb, a);
+                       tb, th, a);
     if (st) return st;
     return cuda_status(cudaGetLastError());
   }
