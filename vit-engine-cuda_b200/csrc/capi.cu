@@ -102,6 +102,14 @@ bool pdl_enabled() {
   return on;
 }
 
+bool tma_store_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VITB200_TMA_STORE");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 int* device_error_word() {
   int st = 0;
   DeviceState* d = device_state(&st);

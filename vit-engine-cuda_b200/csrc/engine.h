@@ -175,6 +175,10 @@ inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? 0 : static_cas
 // griddep_wait in common.cuh); on unless the environment sets VITB200_PDL=0.
 bool pdl_enabled();
 
+// Whether epilogues write their results through TMA tensor stores where they
+// can; on unless the environment sets VITB200_TMA_STORE=0.
+bool tma_store_enabled();
+
 // Launches `kernel` on `s` with the library's launch attributes: programmatic
 // stream serialization (when enabled) and, for cluster_x > 1, a cluster of
 // cluster_x CTAs. Counts the launch; returns a vitb200 status code.

@@ -1065,14 +1065,6 @@ constexpr int kF16PairVariant = 15;
 // Process-wide switches and per-device caches; atomic, since host threads
 // (one per GPU, say) may launch concurrently.
 std::atomic<int> g_forced_variant{0};
-bool tma_store_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("VITB200_TMA_STORE");
-    return !(v != nullptr && v[0] == '0');
-  }();
-  return on;
-}
-
 // Split-K of small single-CTA launches (on unless switched off), and a forced
 // split (0 = the cost model's choice).
 std::atomic<int> g_split_k{1};
