@@ -322,6 +322,17 @@ typedef struct vitb200_block_params {
      * above). 0: TF32 pairs. */
     int attn_f16;
     float q_scale, k_scale, v_scale;
+    /* LayerNorm folded into the GEMM it feeds (used when
+     * vitb200_vit_params.ln_fold != 0; may be NULL otherwise): the FP16
+     * planes of W * diag(gamma) (scale s, *_acc_scale = 2^-11 / s), c[n] =
+     * sum_k W[n][k] gamma[k] and d[n] = sum_k W[n][k] beta[k] + b[n], for qkv
+     * with norm1 and fc1 with norm2. */
+    const uint16_t* ln_qkv_w_f16; float ln_qkv_acc_scale;
+    const float* ln_qkv_c;
+    const float* ln_qkv_d;
+    const uint16_t* ln_fc1_w_f16; float ln_fc1_acc_scale;
+    const float* ln_fc1_c;
+    const float* ln_fc1_d;
 } vitb200_block_params;
 
 typedef struct vitb200_vit_params {
@@ -353,6 +364,15 @@ typedef struct vitb200_vit_params {
      * (code 6, vitb200_device_error) instead of failing silently. */
     const uint16_t* patch_w_f16;
     float patch_acc_scale;
+    /* ln_fold != 0 (every block's ln_* fields set, all four block GEMMs on
+     * FP16 splits): the LayerNorms before qkv and fc1 run inside those GEMMs.
+     * The residual GEMM before each writes, besides x, the FP16 split of x
+     * and per-row statistics over 32-column slabs; the next GEMM multiplies
+     * that split by W * diag(gamma) and its epilogue applies
+     * rstd * (acc - mean * c) + d. The residual stream's magnitudes must then
+     * stay below 32768 (device error 6 otherwise). Replaces 23 of the 24
+     * LayerNorm launches of a ViT-B/16 forward. */
+    int ln_fold;
 } vitb200_vit_params;
 
 /* Workspace needed by vitb200_vit_forward / _features for `batch` images. */

@@ -443,3 +443,66 @@ def test_out_of_range_pixel_reported(case224, cuda):
     assert vit_cuda.device_error(clear=True) == 0
     ref = orc.vit_forward(img, state)
     assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
+
+
+def test_nan_pixel_reported(case224, cuda):
+    """A NaN pixel among finite ones is reported like an out-of-range one
+    (code 6): the range check does not rely on fmaxf, which drops NaN."""
+    import vit_cuda
+    _, _, _, _, model = case224
+    img = synthetic_images(1, 224, seed=10)
+    img[0, 2, 17, 201] = float("nan")
+    with torch.no_grad():
+        model(img.to(cuda))
+    assert vit_cuda.device_error(clear=True) == 6
+
+
+def test_folded_layernorm_matches_unfolded_and_oracle(case224, cuda):
+    """Below 1024 token rows the LayerNorms before qkv and fc1 run inside those
+    GEMMs (vitb200_vit_params.ln_fold): the GEMM multiplies the FP16 split of x
+    by W * diag(gamma) and applies rstd * (acc - mean * c) + d with the row
+    statistics the previous residual GEMM wrote. Both forms meet the parity
+    bars per block (chained) and on the logits, and they differ (the fold ran)
+    only at FP32 rounding level. (test_blocks_chained / _teacher_forced check
+    the folded path per block: the model folds at this batch.)"""
+    state, img, ref, inter, model = case224
+    assert model.ln_folded
+    plain = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()},
+                    ln_fold=False).to(cuda).eval()
+    assert not plain.ln_folded
+    with torch.no_grad():
+        a = model(img.to(cuda)).double().cpu()
+        b = plain(img.to(cuda)).double().cpu()
+    for out in (a, b):
+        assert (out - ref).abs().max().item() <= LOGITS_ATOL
+        assert torch.equal(out.argmax(-1), ref.argmax(-1))
+    assert not torch.equal(a, b)
+    assert (a - b).abs().max().item() <= 1e-4
+    x = plain.embed(img.to(cuda))
+    for i, ref_block in enumerate(inter["blocks"]):
+        x = plain.block(i, x)
+        assert orc.rel_l2(x.cpu(), ref_block) <= BLOCK_REL_L2, i
+
+
+def test_folded_layernorm_range_reported(cuda):
+    """With the LayerNorms folded, the GEMMs read the FP16 split of the
+    residual stream itself, which must stay below 32768 in magnitude: a
+    residual stream past that (patch weights scaled by 2^20) is reported
+    through the device error word (code 6); unfolded, the same model runs and
+    matches the oracle."""
+    import vit_cuda
+    state = synthetic_state_dict(seed=3, img_size=224, depth=2)
+    state["patch_embed.proj.weight"] = state["patch_embed.proj.weight"] * 2.0 ** 20
+    img = synthetic_images(1, 224, seed=4)
+    dev_state = {k: v.to(cuda) for k, v in state.items()}
+    folded = ViTCUDA(state_dict=dev_state).to(cuda).eval()
+    assert folded.ln_folded
+    with torch.no_grad():
+        folded(img.to(cuda))
+    assert vit_cuda.device_error(clear=True) == 6
+    plain = ViTCUDA(state_dict=dev_state, ln_fold=False).to(cuda).eval()
+    with torch.no_grad():
+        out = plain(img.to(cuda)).double().cpu()
+    assert vit_cuda.device_error(clear=True) == 0
+    ref = orc.vit_forward(img, state)
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())

@@ -674,6 +674,11 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
       return VITB200_E_INVALID_ARG;
     if (b.attn_f16 && (!(b.q_scale > 0.f) || !(b.k_scale > 0.f) || !(b.v_scale > 0.f)))
       return VITB200_E_INVALID_ARG;
+    if (p->ln_fold &&
+        (!b.ln_qkv_w_f16 || !b.ln_qkv_c || !b.ln_qkv_d || !(b.ln_qkv_acc_scale > 0.f) ||
+         !b.ln_fc1_w_f16 || !b.ln_fc1_c || !b.ln_fc1_d || !(b.ln_fc1_acc_scale > 0.f) ||
+         !b.proj_w_f16 || !b.fc2_w_f16))
+      return VITB200_E_INVALID_ARG;
   }
   d->P = (p->img_h / 16) * (p->img_w / 16);
   d->T = d->P + 1;
@@ -681,6 +686,17 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
   d->M = static_cast<int64_t>(batch) * d->T;
   d->Mp = static_cast<int64_t>(batch) * d->P;
   return 0;
+}
+
+// Folded LayerNorms pay off only below this many token rows: there the 23
+// LayerNorm launches they save are mostly launch latency, while at batch 256
+// the residual GEMMs' extra split-and-statistics work costs more than the
+// LayerNorm kernels (measured 29.46 vs 28.83 ms per forward on one B200;
+// batch 1: 0.852 vs 0.877 ms). The same threshold picks CTA-pair GEMM tiles.
+constexpr int64_t kLnFoldMaxRows = 1024;
+
+bool use_ln_fold(const vitb200_vit_params* p, const VitDims& d) {
+  return p->ln_fold != 0 && d.M < kLnFoldMaxRows;
 }
 
 // Workspace regions of the forward. x is the residual stream [M][768];
@@ -692,6 +708,9 @@ int check_params(const vitb200_vit_params* p, int batch, VitDims* d) {
 // LN of the CLS rows.
 struct VitBuffers {
   float *x, *pair_a, *qk, *vt, *hpair, *cls_pair;
+  // ln_fold: the FP16 split of x [2][M][768] and its slab statistics [24][M].
+  uint16_t* xs;
+  float2* xstats;
 };
 
 size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve* c,
@@ -706,6 +725,12 @@ size_t carve_vit(const vitb200_vit_params* p, const VitDims& d, int batch, Carve
                            (vt16_halves(batch, d.T, p->num_heads) + 1) / 2));
   b->hpair = c->take(2 * static_cast<size_t>(d.M) * p->mlp_dim);
   b->cls_pair = c->take(2 * static_cast<size_t>(batch) * D);
+  b->xs = nullptr;
+  b->xstats = nullptr;
+  if (use_ln_fold(p, d)) {
+    b->xs = reinterpret_cast<uint16_t*>(c->take(static_cast<size_t>(d.M) * D));
+    b->xstats = reinterpret_cast<float2*>(c->take(2 * static_cast<size_t>(d.M) * (D / 32)));
+  }
   return align_up(c->off, 256);
 }
 
@@ -747,6 +772,135 @@ int vit_embed(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
 // One pre-LN encoder block in place on x (vit_cuda/model.py:39-60 order):
 // x += proj(attn(LN1 x)); x += fc2(GELU(fc1(LN2 x))). Residual adds are fused
 // into the proj / fc2 epilogues.
+//
+// With p->ln_fold the two LayerNorms run inside the GEMMs they feed: qkv and
+// fc1 read the FP16 split of x (b.xs) with W * diag(gamma) and apply
+// rstd * (acc - mean * c) + d in their epilogues from the slab statistics
+// (b.xstats); proj writes that split and those statistics of the new x
+// beside x, and so does fc2 when emit_next (for the next block's qkv).
+// xs_ready: b.xs / b.xstats already hold x's (written by the previous fc2);
+// otherwise one kernel writes them first.
+int vit_block_fold(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, int layer,
+                   float* x, int batch, cudaStream_t s, bool xs_ready, bool emit_next) {
+  const int D = p->embed_dim;
+  const int64_t M = d.M;
+  const int64_t plane = M * D;
+  const int64_t hplane = M * p->mlp_dim;
+  const vitb200_block_params& w = p->blocks[layer];
+  uint16_t* a16 = reinterpret_cast<uint16_t*>(b.pair_a);
+  uint16_t* h16 = reinterpret_cast<uint16_t*>(b.hpair);
+  if (!xs_ready) {
+    if (int st = xsplit_stats_launch(x, D, M, b.xs, D, plane, b.xstats, s)) return st;
+  }
+  // The GEMM feeding from a folded LayerNorm: A = the split of x, bias -> (c, d).
+  auto set_ln = [&](GemmProblem& g, const uint16_t* wf16, float acc, const float* c,
+                    const float* dd) {
+    g.f16 = 1;
+    g.a_h16 = b.xs;
+    g.b_h16 = wf16;
+    g.acc_scale = acc;
+    g.epi.ln_c = c;
+    g.epi.ln_d = dd;
+    g.epi.ln_stats = b.xstats;
+    g.epi.ln_slabs = D / 32;
+    g.epi.ln_eps = p->ln_eps;
+  };
+  // The residual GEMM writing x (and, for the next folded LayerNorm, its split
+  // and statistics).
+  auto set_out = [&](GemmProblem& g, bool emit) {
+    g.epi.residual = x;
+    g.epi.ldr = D;
+    g.epi.out = x;
+    g.epi.ldo = D;
+    if (emit) {
+      g.epi.out_h16 = b.xs;
+      g.epi.ldh = D;
+      g.epi.h16_plane = plane;
+      g.epi.stats_out = b.xstats;
+      g.epi.h16_check = 1;
+    }
+  };
+  const int T8 = (d.T + 7) / 8 * 8;
+  uint16_t* q16 = reinterpret_cast<uint16_t*>(b.qk);
+  uint16_t* k16 = q16 + 2 * plane;
+  uint16_t* vt16 = reinterpret_cast<uint16_t*>(b.vt);
+  {
+    GemmProblem g;
+    set_ln(g, w.ln_qkv_w_f16, w.ln_qkv_acc_scale, w.ln_qkv_c, w.ln_qkv_d);
+    g.M = M;
+    g.N = 3 * D;
+    g.Kp = D;
+    g.epi.e_split = D;
+    g.epi.T = d.T;
+    if (w.attn_f16) {
+      g.epi.mode = kModeQKVAttn16;
+      g.epi.q16 = q16;
+      g.epi.k16 = k16;
+      g.epi.vt16 = vt16;
+      g.epi.vt16_plane = static_cast<int64_t>(vt16_halves(batch, d.T, p->num_heads) / 2);
+      g.epi.T4 = T8;
+      g.epi.q_scale = w.q_scale;
+      g.epi.k_scale = w.k_scale;
+      g.epi.v_scale = w.v_scale;
+    } else {
+      g.epi.mode = kModeQKVAttn;
+      g.epi.out_pair = b.qk;
+      g.epi.ldp = 2 * D;
+      g.epi.pair_plane = M * 2 * D;
+      g.epi.T4 = (d.T + 3) / 4 * 4;
+      g.epi.vt_pair = b.vt;
+      g.epi.vt_plane = static_cast<int64_t>(vt_pair_floats(batch, d.T, p->num_heads) / 2);
+    }
+    if (int st = gemm_pairs_launch(g, s)) return st;
+  }
+  if (w.attn_f16) {
+    if (int st = attention_f16_launch(q16, k16, D, vt16, T8, nullptr, 0, nullptr, D, plane, a16, D,
+                                      plane, batch, d.T, p->num_heads, p->attn_scale, w.q_scale,
+                                      w.k_scale, w.v_scale, s))
+      return st;
+  } else if (int st = attention_launch(b.qk, 2 * D, 0, b.qk, 2 * D, D, b.vt, nullptr, 0, nullptr,
+                                       D, plane, batch, d.T, p->num_heads, p->attn_scale, s, a16,
+                                       D, plane)) {
+    return st;
+  }
+  {
+    GemmProblem g;
+    g.f16 = 1;
+    g.a_h16 = a16;
+    g.b_h16 = w.proj_w_f16;
+    g.acc_scale = w.proj_acc_scale;
+    g.M = M;
+    g.N = D;
+    g.Kp = D;
+    g.epi.bias = w.proj_b;
+    set_out(g, true);
+    if (int st = gemm_pairs_launch(g, s)) return st;
+  }
+  {
+    GemmProblem g;
+    set_ln(g, w.ln_fc1_w_f16, w.ln_fc1_acc_scale, w.ln_fc1_c, w.ln_fc1_d);
+    g.M = M;
+    g.N = p->mlp_dim;
+    g.Kp = D;
+    g.epi.gelu = 1;
+    g.epi.out_h16 = h16;
+    g.epi.ldh = p->mlp_dim;
+    g.epi.h16_plane = hplane;
+    if (int st = gemm_pairs_launch(g, s)) return st;
+  }
+  GemmProblem g;
+  g.f16 = 1;
+  g.a_h16 = h16;
+  g.b_h16 = w.fc2_w_f16;
+  g.acc_scale = w.fc2_acc_scale;
+  g.M = M;
+  g.N = D;
+  g.Kp = p->mlp_dim;
+  g.epi.bias = w.fc2_b;
+  set_out(g, emit_next);
+  return gemm_pairs_launch(g, s);
+}
+
 int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, int layer,
               float* x, int batch, cudaStream_t s) {
   const int D = p->embed_dim;
@@ -870,6 +1024,19 @@ int vit_block(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b
   return gemm_pairs_launch(g, s);
 }
 
+// The encoder blocks in order; with folded LayerNorms each fc2 hands the next
+// block's qkv the split and statistics of x.
+int vit_blocks(const vitb200_vit_params* p, const VitDims& d, const VitBuffers& b, float* x,
+               int batch, cudaStream_t s) {
+  const bool fold = use_ln_fold(p, d);
+  for (int i = 0; i < p->depth; ++i) {
+    const int st = fold ? vit_block_fold(p, d, b, i, x, batch, s, i > 0, i + 1 < p->depth)
+                        : vit_block(p, d, b, i, x, batch, s);
+    if (st) return st;
+  }
+  return 0;
+}
+
 // Final LayerNorm on the CLS rows only (the head reads token 0 alone) and the
 // head: one fused kernel (CUDA-core FP32 dot products, batch invariant; at
 // batch 1 a head GEMM launch is all latency), with LayerNorm + head GEMM for
@@ -934,8 +1101,7 @@ int vitb200_vit_forward(const vitb200_vit_params* p, const float* img, float* lo
   if (batch == 0) return 0;
   cudaStream_t s = as_stream(stream);
   if (int st = vit_embed(p, d, b, img, b.x, batch, s)) return st;
-  for (int i = 0; i < p->depth; ++i)
-    if (int st = vit_block(p, d, b, i, b.x, batch, s)) return st;
+  if (int st = vit_blocks(p, d, b, b.x, batch, s)) return st;
   return vit_head(p, d, b, b.x, logits, nullptr, batch, s);
   VITB200_GUARD_END
 }
@@ -951,8 +1117,7 @@ int vitb200_vit_forward_features(const vitb200_vit_params* p, const float* img, 
   if (batch == 0) return 0;
   cudaStream_t s = as_stream(stream);
   if (int st = vit_embed(p, d, b, img, b.x, batch, s)) return st;
-  for (int i = 0; i < p->depth; ++i)
-    if (int st = vit_block(p, d, b, i, b.x, batch, s)) return st;
+  if (int st = vit_blocks(p, d, b, b.x, batch, s)) return st;
   return vit_head(p, d, b, b.x, nullptr, features, batch, s);
   VITB200_GUARD_END
 }
@@ -977,6 +1142,8 @@ int vitb200_vit_block(const vitb200_vit_params* p, int layer, float* x, int batc
   VitBuffers b;
   if (int st = vit_prepare(p, batch, workspace, workspace_bytes, &d, &b)) return st;
   if (batch == 0) return 0;
+  if (use_ln_fold(p, d))
+    return vit_block_fold(p, d, b, layer, x, batch, as_stream(stream), false, false);
   return vit_block(p, d, b, layer, x, batch, as_stream(stream));
   VITB200_GUARD_END
 }

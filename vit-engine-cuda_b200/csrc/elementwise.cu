@@ -217,6 +217,73 @@ __global__ void __launch_bounds__(256) layernorm768_kernel(
   }
 }
 
+// The input of a LayerNorm folded into the next GEMM (vit_params.ln_fold): per
+// 768-wide row, its FP16 split (planes h16[2][rows][hld]: hi, lo*2^11; a
+// magnitude of 32768 or more sets the device error) and, per 32-column slab,
+// (sum, M2 about the slab's mean) into stats[slab][rows]. One warp per row:
+// lane l holds float4 columns l + 32 i, so slab 4 i + l / 8 lies on eight
+// lanes, reduced by three shuffles.
+__global__ void __launch_bounds__(256) xsplit_stats768_kernel(
+    const float* __restrict__ x, int64_t ldx, int64_t rows, uint16_t* __restrict__ h16,
+    int64_t hld, int64_t hplane, float2* __restrict__ stats, int* err) {
+  griddep_wait();
+  griddep_launch_dependents();
+  constexpr int V = 6;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = warp_global; r < rows; r += nwarps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
+    float4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+    float mx = 0.f, nan = 0.f;  // fmaxf drops NaN; a sum carries it
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 o = v[i];
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+      float sum = (o.x + o.y) + (o.z + o.w);
+      nan += sum - sum;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      const float mean = sum * (1.f / 32.f);
+      const float a0 = o.x - mean, a1 = o.y - mean, a2 = o.z - mean, a3 = o.w - mean;
+      float m2 = (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+      m2 += __shfl_xor_sync(0xffffffffu, m2, 1);
+      m2 += __shfl_xor_sync(0xffffffffu, m2, 2);
+      m2 += __shfl_xor_sync(0xffffffffu, m2, 4);
+      if ((lane & 7) == 0) stats[static_cast<int64_t>(4 * i + lane / 8) * rows + r] = make_float2(sum, m2);
+      const int col = (lane + 32 * i) * 4;
+      __half h0, h1, h2, h3, l0, l1, l2, l3;
+      h16_split(o.x, h0, l0);
+      h16_split(o.y, h1, l1);
+      h16_split(o.z, h2, l2);
+      h16_split(o.w, h3, l3);
+      *reinterpret_cast<uint2*>(h16 + r * hld + col) = make_uint2(pack_h2(h0, h1), pack_h2(h2, h3));
+      *reinterpret_cast<uint2*>(h16 + hplane + r * hld + col) =
+          make_uint2(pack_h2(l0, l1), pack_h2(l2, l3));
+    }
+    if (!(mx < kH16Limit && nan == 0.f)) report_error(err, kErrF16Range);
+  }
+}
+
+int xsplit_stats_launch(const float* x, int64_t ldx, int64_t rows, uint16_t* h16, int64_t hld,
+                        int64_t hplane, float2* stats, cudaStream_t s) {
+  if (rows < 0 || !x || !h16 || !stats) return VITB200_E_INVALID_ARG;
+  if (rows == 0) return 0;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || ldx % 4 || reinterpret_cast<uintptr_t>(h16) % 8 ||
+      hld % 4 || hplane % 4 || reinterpret_cast<uintptr_t>(stats) % 8)
+    return VITB200_E_ALIGNMENT;
+  int* err = device_error_word();
+  if (err == nullptr) return VITB200_E_INVALID_ARG;
+  const int threads = 256;
+  if (int st_ = launch_kernel(xsplit_stats768_kernel, dim3(grid_for(rows * 32, threads)),
+                             dim3(threads), 0, s, 1, x, ldx, rows, h16, hld, hplane, stats, err))
+    return st_;
+  return cuda_status(cudaGetLastError());
+}
+
 // Final LayerNorm of each image's CLS row fused with the classifier head. A
 // block serves kHeadImages images and kHeadClasses classes: every warp loads
 // its class's head row (the TF32 pair, hi + lo is w to 2^-22) into registers
@@ -421,8 +488,10 @@ __global__ void im2col_pair_kernel(const float* __restrict__ img, int B, int C, 
       uint32_t h0, l0, h1, l1;
       h16_split2(v.x, v.y, h0, l0);
       h16_split2(v.z, v.w, h1, l1);
+      // fmaxf drops NaN; the sum carries it (and turns inf - inf into NaN).
       const float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-      if (!(mx < kH16Limit)) report_error(err, kErrF16Range);
+      const float sum = (v.x + v.y) + (v.z + v.w);
+      if (!(mx < kH16Limit && sum == sum)) report_error(err, kErrF16Range);
       uint16_t* dst = h16 + m * K + k;
       *reinterpret_cast<uint2*>(dst) = make_uint2(h0, h1);
       *reinterpret_cast<uint2*>(dst + plane) = make_uint2(l0, l1);

@@ -48,6 +48,22 @@ struct GemmEpilogue {
   uint16_t* vt16 = nullptr;
   int64_t vt16_plane = 0;           // elements between vt16 planes
   float q_scale = 1.f, k_scale = 1.f, v_scale = 1.f;  // powers of two
+  // LayerNorm folded into this GEMM: A is the FP16 split of the rows x before
+  // normalisation and B the planes of W * diag(gamma); the result is
+  // rstd * (acc - mean * ln_c[n]) + ln_d[n] (in place of the bias), the row's
+  // mean and 1 / sqrt(var + ln_eps) combined from ln_stats[s][m] = (sum, M2)
+  // over the ln_slabs 32-column slabs of the row.
+  const float* ln_c = nullptr;
+  const float* ln_d = nullptr;
+  const float2* ln_stats = nullptr;
+  int ln_slabs = 0;
+  float ln_eps = 0.f;
+  // Statistics of the result for a LayerNorm folded into the next GEMM:
+  // stats_out[n / 32][m] = (sum, M2 about the slab's mean) of each row's
+  // 32-column slab; with h16_check, a result (its FP16 split in out_h16)
+  // of magnitude 32768 or more sets the device error.
+  float2* stats_out = nullptr;
+  int h16_check = 0;
 };
 
 struct GemmProblem {
@@ -174,6 +190,12 @@ inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? 0 : static_cas
 // Whether kernels are launched with programmatic stream serialization (see
 // griddep_wait in common.cuh); on unless the environment sets VITB200_PDL=0.
 bool pdl_enabled();
+
+// FP16 split of x[rows][768] (planes [2][rows][hld]) and its per-row
+// statistics over 32-column slabs, stats[24][rows] = (sum, M2): the input of
+// a LayerNorm folded into the next GEMM. Returns a vitb200 status code.
+int xsplit_stats_launch(const float* x, int64_t ldx, int64_t rows, uint16_t* h16, int64_t hld,
+                        int64_t hplane, float2* stats, cudaStream_t s);
 
 // Whether epilogues write their results through TMA tensor stores where they
 // can; on unless the environment sets VITB200_TMA_STORE=0.

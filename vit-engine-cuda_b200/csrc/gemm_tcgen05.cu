@@ -73,11 +73,15 @@ struct GemmArgs {
                    // out_h16 (planes 0-1), or q16 | k16 (planes 0-1 | 2-3)
   int tma_out;     // the fp32 result goes out through tmap_h (TMA stores), and the
                    // residual (the same tensor) comes in through it (TMA loads)
+  int tma_h16b;    // with tma_out: the FP16 split of the result through tmap_h2
   int* err;
   GemmEpilogue epi;
 };
 
 constexpr int kBM = 128;
+// Folded LayerNorm: the most 32-column slabs a row's statistics come in
+// (768 / 32; a multiple of 4).
+constexpr int kMaxLnSlabs = 24;
 // Epilogue transpose buffer of one warp: 32 rows x 32 words (pitch 32); the
 // 16-byte chunk q of row r sits at chunk position q ^ (r & 7), so a lane
 // writing its own row and eight lanes reading one row both touch eight
@@ -227,11 +231,29 @@ __device__ __forceinline__ void h16_slab_store_tma(const float (&v)[32], float* 
 
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err);
 
+// Row statistics (count 32, sum, M2 about the mean) of one lane's 32 values,
+// four independent chains each.
+__device__ __forceinline__ float2 slab_stats(const float (&v)[32]) {
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s4[j & 3] += v[j];
+  const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  const float mean = sum * (1.f / 32.f);
+  float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float d = v[j] - mean;
+    q4[j & 3] = fmaf(d, d, q4[j & 3]);
+  }
+  return make_float2(sum, (q4[0] + q4[1]) + (q4[2] + q4[3]));
+}
+
 template <bool F16>
 __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base, int lane, int n0,
                                               float (&v)[32], float* stg,
-                                              const CUtensorMap* tmap_h, uint64_t* res_bar,
-                                              uint32_t& res_phase) {
+                                              const CUtensorMap* tmap_h,
+                                              const CUtensorMap* tmap_h2, uint64_t* res_bar,
+                                              uint32_t& res_phase, float ln_mu, float ln_rstd) {
   const GemmEpilogue& e = a.epi;
   const int N = a.N;
   const int64_t m = m_base + lane;
@@ -241,7 +263,28 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
   // Undo the operand scales (FP16 kinds; a power of two, so the product is
   // exact) and add the bias: one rounding, as acc * scale + bias would give.
   const float sc = F16 ? a.acc_scale : 1.f;
-  if (e.bias != nullptr) {
+  if (e.ln_c != nullptr) {
+    // LayerNorm folded in: rstd * (acc - mean * c) + d.
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(e.ln_c + n0 + j));
+        const float4 d4 = __ldg(reinterpret_cast<const float4*>(e.ln_d + n0 + j));
+        v[j] = fmaf(ln_rstd, fmaf(-ln_mu, c4.x, v[j] * sc), d4.x);
+        v[j + 1] = fmaf(ln_rstd, fmaf(-ln_mu, c4.y, v[j + 1] * sc), d4.y);
+        v[j + 2] = fmaf(ln_rstd, fmaf(-ln_mu, c4.z, v[j + 2] * sc), d4.z);
+        v[j + 3] = fmaf(ln_rstd, fmaf(-ln_mu, c4.w, v[j + 3] * sc), d4.w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = n0 + j;
+        const float c = n < N ? __ldg(e.ln_c + n) : 0.f;
+        const float d = n < N ? __ldg(e.ln_d + n) : 0.f;
+        v[j] = fmaf(ln_rstd, fmaf(-ln_mu, c, v[j] * sc), d);
+      }
+    }
+  } else if (e.bias != nullptr) {
     if (full && a.vec_bias) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
@@ -423,9 +466,26 @@ __device__ __forceinline__ void epilogue_slab(const GemmArgs& a, int64_t m_base,
       }
       flush(e.out_pair + e.pair_plane, e.ldp);
     }
+    if (e.stats_out != nullptr) {
+      const float2 st = slab_stats(v);
+      if (m < a.M) e.stats_out[static_cast<int64_t>(n0 / 32) * a.M + m] = st;
+      if (e.h16_check) {
+        // fmaxf drops NaN; the slab's sum carries it.
+        float mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, fabsf(v[j]));
+        if (row_ok && !(mx < kH16Limit && st.x == st.x)) report_error(a.err, kErrF16Range);
+      }
+    }
     if (e.out_h16 != nullptr) {
+      if (a.tma_out) {  // the fp32 store must have read the buffer
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+      }
       if (a.tma_h16)
         h16_slab_store_tma(v, stg, lane, m_base, col_base, tmap_h, 0);
+      else if (a.tma_h16b)
+        h16_slab_store_tma(v, stg, lane, m_base, col_base, tmap_h2, 0);
       else
         h16_slab_store(v, stg, lane, m_base, a.M, e.out_h16, e.ldh, e.h16_plane, col_base);
     }
@@ -582,7 +642,8 @@ template <int KIND, int BN, int BK, int STAGES, int CHUNK_KB, bool PAIR, int EPI
 __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b,
-                       const __grid_constant__ CUtensorMap tmap_h, const GemmArgs args) {
+                       const __grid_constant__ CUtensorMap tmap_h,
+                       const __grid_constant__ CUtensorMap tmap_h2, const GemmArgs args) {
   using Cfg = GemmCfg<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>;
   using Epi = EpiCfg<EPI>;
   constexpr bool F16 = Cfg::F16;
@@ -840,6 +901,49 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       const int split = w - tile * ksplit;
       const int m_blk = tile / args.num_n_tiles;
       const int n_blk = tile - m_blk * args.num_n_tiles;
+      // Folded LayerNorm: this row's mean and 1 / sqrt(var + eps), combined
+      // from its slabs' (sum, M2) as Chan et al.'s parallel variance (every
+      // slab holds 32 values: M2 = sum_s M2_s + 32 (m_s - mean)^2). Computed
+      // before the accumulator is drained, so the loads overlap the MMAs; all
+      // of a row's slabs (up to kMaxLnSlabs) are loaded at once.
+      float ln_mu = 0.f, ln_rstd = 0.f;
+      if (args.epi.ln_c != nullptr) {
+        const int64_t m_row = static_cast<int64_t>(m_blk) * Cfg::kTileM +
+                              static_cast<int64_t>(rank) * kBM + quarter * 32 + lane;
+        if (m_row < args.M) {
+          const float2* st = args.epi.ln_stats + m_row;
+          const int slabs = args.epi.ln_slabs;
+          float2 pr[kMaxLnSlabs];
+#pragma unroll
+          for (int sl = 0; sl < kMaxLnSlabs; ++sl)
+            pr[sl] = sl < slabs ? st[static_cast<int64_t>(sl) * args.M] : make_float2(0.f, 0.f);
+          float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+#pragma unroll
+          for (int sl = 0; sl < kMaxLnSlabs; sl += 4) {
+            t0 += pr[sl].x;
+            t1 += pr[sl + 1].x;
+            t2 += pr[sl + 2].x;
+            t3 += pr[sl + 3].x;
+          }
+          const float n = 32.f * static_cast<float>(slabs);
+          const float mean = ((t0 + t1) + (t2 + t3)) / n;
+          float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
+          auto acc = [&](float& q, float2 p2, bool valid) {
+            const float d = fmaf(p2.x, 1.f / 32.f, -mean);
+            if (valid) q += fmaf(32.f * d, d, p2.y);
+          };
+#pragma unroll
+          for (int sl = 0; sl < kMaxLnSlabs; sl += 4) {
+            acc(q0, pr[sl], sl < slabs);
+            acc(q1, pr[sl + 1], sl + 1 < slabs);
+            acc(q2, pr[sl + 2], sl + 2 < slabs);
+            acc(q3, pr[sl + 3], sl + 3 < slabs);
+          }
+          const float var = ((q0 + q1) + (q2 + q3)) / n;
+          ln_mu = mean;
+          ln_rstd = 1.0f / sqrtf(var + args.epi.ln_eps);
+        }
+      }
       float sum[Cfg::kWgCols];
 #pragma unroll
       for (int c = 0; c < Cfg::kWgCols; ++c) sum[c] = 0.f;
@@ -949,8 +1053,8 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
           const int n0 = n_blk * BN + slab * 32;
           if ((Cfg::kSlabs % EPI == 0 || slab < Cfg::kSlabs) && n0 < args.N) {
             float(&part)[32] = *reinterpret_cast<float(*)[32]>(&sum[0]);
-            epilogue_slab<F16>(args, m_base, lane, n0, part, stg, &tmap_h, &res_bar[warp - 4],
-                               res_phase);
+            epilogue_slab<F16>(args, m_base, lane, n0, part, stg, &tmap_h, &tmap_h2,
+                               &res_bar[warp - 4], res_phase, ln_mu, ln_rstd);
           }
           if (i + 1 < Cfg::kWgSlabs) {
 #pragma unroll
@@ -960,7 +1064,7 @@ __global__ void __launch_bounds__(EpiCfg<EPI>::kThreads, 1)
       }
     }
     // TMA stores of the result complete before the CTA can exit.
-    if ((args.tma_h16 || args.tma_out) && lane == 0) bulk_wait_group<0>();
+    if ((args.tma_h16 || args.tma_out || args.tma_h16b) && lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -1168,10 +1272,12 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
   // (box {32 columns, 32 rows, 2 planes}, 64-byte swizzle): the split as the
   // only output (fc1's H), and the q and k splits of the QKV epilogue when k16
   // directly follows q16's two planes.
-  CUtensorMap th;
+  CUtensorMap th, th2;
   std::memset(&th, 0, sizeof(th));
+  std::memset(&th2, 0, sizeof(th2));
   a.tma_h16 = 0;
   a.tma_out = 0;
+  a.tma_h16b = 0;
   if (tma_store_enabled()) {
     const uint32_t box[3] = {32, 32, 2};
     if (e.out_h16 != nullptr && a.vec_h16 && e.out == nullptr && e.out_pair == nullptr &&
@@ -1187,17 +1293,25 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
       const uint64_t strides[2] = {E * 2, static_cast<uint64_t>(p.M) * E * 2};
       if (int st2 = encode_tmap_typed(&th, 3, e.q16, dims, strides, box, 0, 1)) return st2;
       a.tma_h16 = 1;
-    } else if (e.out != nullptr && a.vec_out && e.out_pair == nullptr && e.out_h16 == nullptr &&
+    } else if (e.out != nullptr && a.vec_out && e.out_pair == nullptr &&
                e.mode == kModePlain && p.N % 32 == 0 &&
                (e.residual == nullptr || (e.residual == e.out && e.ldr == e.ldo))) {
       // The fp32 result (and the residual it replaces), box {32 columns, 32
-      // rows}: the transpose buffer's layout is the map's 128-byte swizzle.
+      // rows}: the transpose buffer's layout is the map's 128-byte swizzle;
+      // an FP16 split of the same result through the second map.
       const uint64_t dims[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), 1};
       const uint64_t strides[2] = {static_cast<uint64_t>(e.ldo) * 4,
                                    static_cast<uint64_t>(e.ldo) * 4 * static_cast<uint64_t>(p.M)};
       const uint32_t box32[3] = {32, 32, 1};
       if (int st2 = encode_tmap_typed(&th, 3, e.out, dims, strides, box32, 1, 0)) return st2;
       a.tma_out = 1;
+      if (e.out_h16 != nullptr && a.vec_h16) {
+        const uint64_t hd[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), 2};
+        const uint64_t hs[2] = {static_cast<uint64_t>(e.ldh) * 2,
+                                static_cast<uint64_t>(e.h16_plane) * 2};
+        if (int st2 = encode_tmap_typed(&th2, 3, e.out_h16, hd, hs, box, 0, 1)) return st2;
+        a.tma_h16b = 1;
+      }
     }
   }
   if constexpr (PAIR) {
@@ -1227,7 +1341,7 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
     }
     const dim3 grid(2 * static_cast<unsigned>(std::min<int64_t>(tiles, slots)));
     st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
-                       dim3(kThreads), Cfg::kSmemBytes, s, 2, ta, tb, th, a);
+                       dim3(kThreads), Cfg::kSmemBytes, s, 2, ta, tb, th, th2, a);
     if (st) return st;
     return cuda_status(cudaGetLastError());
   } else {
@@ -1236,7 +1350,7 @@ int launch_variant(const GemmProblem& p, int ksplit, int* err, cudaStream_t s) {
         a.ksplit > 1 ? tiles * a.ksplit : std::min<int64_t>(tiles, device_num_sms())));
     st = launch_kernel(gemm_tf32x3_kernel<KIND, BN, BK, STAGES, CHUNK_KB, PAIR, EPI>, grid,
                        dim3(kThreads), Cfg::kSmemBytes, s, static_cast<unsigned>(a.ksplit), ta,
-                       tb, th, a);
+                       tb, th, th2, a);
     if (st) return st;
     return cuda_status(cudaGetLastError());
   }
@@ -1401,6 +1515,18 @@ int gemm_pairs_launch(const GemmProblem& p, cudaStream_t s) {
        p.epi.residual || p.epi.gelu || p.epi.T <= 0 || p.epi.T4 < p.epi.T || p.epi.T4 % 8 ||
        reinterpret_cast<uintptr_t>(p.epi.q16) % 16 || reinterpret_cast<uintptr_t>(p.epi.k16) % 16))
     return VITB200_E_INVALID_ARG;
+  // Folded LayerNorm and row statistics: whole 32-column slabs, written by the
+  // staged epilogue (16-byte aligned rows).
+  if (p.epi.ln_c != nullptr && (!p.epi.ln_d || !p.epi.ln_stats || p.epi.ln_slabs <= 0 ||
+                                p.epi.ln_slabs > kMaxLnSlabs || p.epi.bias || p.Kp == 0))
+    return VITB200_E_INVALID_ARG;
+  if (p.epi.stats_out != nullptr &&
+      (p.N % 32 || !p.epi.out || reinterpret_cast<uintptr_t>(p.epi.out) % 16 || p.epi.ldo % 4 ||
+       (p.epi.residual && (reinterpret_cast<uintptr_t>(p.epi.residual) % 16 || p.epi.ldr % 4)) ||
+       (p.epi.out_h16 && (reinterpret_cast<uintptr_t>(p.epi.out_h16) % 16 || p.epi.ldh % 8 ||
+                          p.epi.h16_plane % 8)) ||
+       p.epi.out_pair || p.epi.mode != kModePlain || p.Kp == 0))
+    return VITB200_E_UNSUPPORTED;
   if (p.Kp == 0) return gemm_k0_launch(p, s);
   const void* a_ptr = f16 ? static_cast<const void*>(p.a_h16) : p.a_pair;
   const void* b_ptr = f16 ? static_cast<const void*>(p.b_h16) : p.b_pair;

@@ -47,7 +47,11 @@ class BlockParams(ctypes.Structure):
         ("proj_w_f16", c_void_p), ("proj_acc_scale", c_float),
         ("fc1_w_f16", c_void_p), ("fc1_acc_scale", c_float),
         ("fc2_w_f16", c_void_p), ("fc2_acc_scale", c_float),
-        ("attn_f16", c_int), ("q_scale", c_float), ("k_scale", c_float), ("v_scale", c_float)]
+        ("attn_f16", c_int), ("q_scale", c_float), ("k_scale", c_float), ("v_scale", c_float),
+        ("ln_qkv_w_f16", c_void_p), ("ln_qkv_acc_scale", c_float),
+        ("ln_qkv_c", c_void_p), ("ln_qkv_d", c_void_p),
+        ("ln_fc1_w_f16", c_void_p), ("ln_fc1_acc_scale", c_float),
+        ("ln_fc1_c", c_void_p), ("ln_fc1_d", c_void_p)]
 
 
 class VitParams(ctypes.Structure):
@@ -60,6 +64,7 @@ class VitParams(ctypes.Structure):
         ("norm_w", c_void_p), ("norm_b", c_void_p),
         ("head_w_pair", c_void_p), ("head_b", c_void_p),
         ("patch_w_f16", c_void_p), ("patch_acc_scale", c_float),
+        ("ln_fold", c_int),
     ]
 
 

@@ -79,11 +79,16 @@ def _split_pair(w: torch.Tensor) -> torch.Tensor:
 
 
 class ViTCUDA(nn.Module):
-    def __init__(self, num_classes=1000, state_dict=None, pretrained=True, operands="auto"):
+    def __init__(self, num_classes=1000, state_dict=None, pretrained=True, operands="auto",
+                 ln_fold=True):
         super().__init__()
         if operands not in ("auto", "tf32"):
             raise ValueError("operands must be 'auto' or 'tf32'")
         self.operands = operands
+        # Fold the LayerNorms before qkv and fc1 into those GEMMs when every
+        # block GEMM runs on FP16 splits (vitb200_vit_params.ln_fold): the
+        # residual stream's magnitudes must then stay below 32768.
+        self.ln_fold = bool(ln_fold)
         if state_dict is None:
             try:
                 import timm  # noqa: F401  (reference model.py:67-69)
@@ -164,6 +169,29 @@ class ViTCUDA(nn.Module):
             attn_f16 = (self.operands == "auto" and bounds["q"] < F16_SAFE_BOUND
                         and bounds["k"] < F16_SAFE_BOUND and bounds["v"] < F16_SAFE_BOUND)
             meta[f"blocks.{i}.attn"] = "f16" if attn_f16 else "tf32"
+        fold = self.ln_fold and self.operands == "auto" and all(
+            meta[f"blocks.{i}.{n}"] == "f16" for i in range(len(self.blocks))
+            for n in ("qkv", "proj", "fc1", "fc2"))
+        folded = {}
+        for i, blk in enumerate(self.blocks if fold else []):
+            for name, gamma, beta in (("qkv", blk.norm1_gamma, blk.norm1_beta),
+                                      ("fc1", blk.norm2_gamma, blk.norm2_beta)):
+                wt = getattr(blk, f"{name}_weight")
+                b = getattr(blk, f"{name}_bias")
+                wg = (wt * gamma.reshape(1, -1)).contiguous()
+                if not f16_weight_ok(wg):
+                    fold = False
+                    break
+                key = f"blocks.{i}.ln_{name}"
+                folded[key + ".f16"], acc_scale = f16_weight(wg)
+                folded[key + ".c"] = (wt.double() @ gamma.double()).float().contiguous()
+                folded[key + ".d"] = (wt.double() @ beta.double() + b.double()).float().contiguous()
+                meta[key + ".acc_scale"] = repr(acc_scale)
+            if not fold:
+                break
+        if fold:
+            tensors.update(folded)
+        meta["ln_fold"] = "1" if fold else "0"
         return tensors, meta
 
     def export_splits(self) -> tuple[dict, dict]:
@@ -221,13 +249,23 @@ class ViTCUDA(nn.Module):
                         blk.norm2_gamma, blk.norm2_beta, blk.fc1_bias, blk.fc2_bias]
                 vecs = [v.contiguous() for v in vecs]
                 keep += vecs
+                ln = {}
+                for name in ("qkv", "fc1"):
+                    key_ = f"blocks.{i}.ln_{name}"
+                    if meta.get("ln_fold") == "1":
+                        ln[name] = (splits[key_ + ".f16"], float(meta[key_ + ".acc_scale"]),
+                                    splits[key_ + ".c"], splits[key_ + ".d"])
+                    else:
+                        ln[name] = (None, 0.0, None, None)
                 blocks[i] = BlockParams(
                     vecs[0].data_ptr(), vecs[1].data_ptr(), ptr(w["qkv"][0]), vecs[2].data_ptr(),
                     ptr(w["proj"][0]), vecs[3].data_ptr(), vecs[4].data_ptr(), vecs[5].data_ptr(),
                     ptr(w["fc1"][0]), vecs[6].data_ptr(), ptr(w["fc2"][0]), vecs[7].data_ptr(),
                     ptr(w["qkv"][1]), w["qkv"][2], ptr(w["proj"][1]), w["proj"][2],
                     ptr(w["fc1"][1]), w["fc1"][2], ptr(w["fc2"][1]), w["fc2"][2],
-                    1 if attn_f16 else 0, 1.0, 1.0, 1.0)
+                    1 if attn_f16 else 0, 1.0, 1.0, 1.0,
+                    ptr(ln["qkv"][0]), ln["qkv"][1], ptr(ln["qkv"][2]), ptr(ln["qkv"][3]),
+                    ptr(ln["fc1"][0]), ln["fc1"][1], ptr(ln["fc1"][2]), ptr(ln["fc1"][3]))
             vecs = {n: getattr(self, n).contiguous() for n in
                     ("patch_bias", "cls_token", "pos_embed", "norm_gamma", "norm_beta",
                      "head_bias")}
@@ -245,7 +283,8 @@ class ViTCUDA(nn.Module):
                 head_w_pair=splits["head.pair"].data_ptr(), head_b=vecs["head_bias"].data_ptr(),
                 patch_w_f16=ptr(splits.get("patch.f16")),
                 patch_acc_scale=(float(meta["patch.acc_scale"])
-                                 if meta.get("patch", "tf32") == "f16" else 0.0))
+                                 if meta.get("patch", "tf32") == "f16" else 0.0),
+                ln_fold=1 if meta.get("ln_fold") == "1" else 0)
             self.patch_operands = meta.get("patch", "tf32")
             if self.head_weight.shape[0] != self.num_classes:
                 raise RuntimeError("head weight rows must equal num_classes")
@@ -255,6 +294,12 @@ class ViTCUDA(nn.Module):
     @property
     def params(self) -> VitParams:
         return self.prepare()[2]
+
+    @property
+    def ln_folded(self) -> bool:
+        """Whether launches below 1024 token rows fold the LayerNorms before
+        qkv and fc1 into those GEMMs (vitb200_vit_params.ln_fold)."""
+        return self.prepare()[5].get("ln_fold") == "1"
 
     def workspace_bytes(self, batch: int) -> int:
         return int(lib.vitb200_vit_workspace_bytes(ctypes.byref(self.params), int(batch)))
