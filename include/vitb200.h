@@ -365,13 +365,15 @@ typedef struct vitb200_vit_params {
     const uint16_t* patch_w_f16;
     float patch_acc_scale;
     /* ln_fold != 0 (every block's ln_* fields set, all four block GEMMs on
-     * FP16 splits): the LayerNorms before qkv and fc1 run inside those GEMMs.
+     * FP16 splits): in launches of fewer than 1024 token rows (up to 5 images
+     * at 224x224) the LayerNorms before qkv and fc1 run inside those GEMMs.
      * The residual GEMM before each writes, besides x, the FP16 split of x
      * and per-row statistics over 32-column slabs; the next GEMM multiplies
      * that split by W * diag(gamma) and its epilogue applies
      * rstd * (acc - mean * c) + d. The residual stream's magnitudes must then
      * stay below 32768 (device error 6 otherwise). Replaces 23 of the 24
-     * LayerNorm launches of a ViT-B/16 forward. */
+     * LayerNorm launches of a ViT-B/16 forward; larger launches keep the
+     * LayerNorm kernel (faster there). */
     int ln_fold;
 } vitb200_vit_params;
 
