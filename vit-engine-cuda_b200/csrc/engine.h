@@ -60,8 +60,8 @@ struct GemmEpilogue {
   float ln_eps = 0.f;
   // Statistics of the result for a LayerNorm folded into the next GEMM:
   // stats_out[n / 32][m] = (sum, M2 about the slab's mean) of each row's
-  // 32-column slab; with h16_check, a result (its FP16 split in out_h16)
-  // of magnitude 32768 or more sets the device error.
+  // 32-column slab; with stats_out and h16_check, a result (its FP16 split in
+  // out_h16) of magnitude 32768 or more, or NaN, sets the device error.
   float2* stats_out = nullptr;
   int h16_check = 0;
 };
