@@ -506,3 +506,26 @@ def test_folded_layernorm_range_reported(cuda):
     assert vit_cuda.device_error(clear=True) == 0
     ref = orc.vit_forward(img, state)
     assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
+
+
+def test_folded_layernorm_with_tf32_attention(cuda):
+    """Folded LayerNorms with one block's attention on TF32 pairs: its q rows of
+    the qkv weight scaled by 2^12 take q's bound past the FP16 split's range
+    (attention -> TF32) while every GEMM input stays inside it (all four GEMMs
+    FP16, so the fold applies). Batch 1 (below 1024 token rows) against the
+    oracle."""
+    state = synthetic_state_dict(seed=6, img_size=224, depth=3)
+    w = state["blocks.1.attn.qkv.weight"].clone()
+    w[:768] *= 2.0 ** 12
+    state["blocks.1.attn.qkv.weight"] = w
+    img = synthetic_images(1, 224, seed=6)
+    ref = orc.vit_forward(img, state)
+    model = ViTCUDA(state_dict={k: v.to(cuda) for k, v in state.items()}).to(cuda).eval()
+    model.prepare()
+    assert model.gemm_operands[1] == {"qkv": "f16", "proj": "f16", "fc1": "f16", "fc2": "f16",
+                                      "attn": "tf32"}
+    assert model.ln_folded
+    with torch.no_grad():
+        out = model(img.to(cuda)).double().cpu()
+    assert (out - ref).abs().max().item() <= LOGITS_ATOL * max(1.0, ref.abs().max().item())
+    assert torch.equal(out.argmax(-1), ref.argmax(-1))
